@@ -1,0 +1,493 @@
+"""Benchmark of the B200 NVFP4 GEMM (BASELINE.json metric: NVFP4 GEMM us and PFLOP/s per B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--size S] [--out-dtype bf16|fp16]
+                    [--impl ours|reference] [--allgather] [--no-e2e] [--no-cpu-baseline]
+
+A step is one GEMM over one batch of synthetic input. The default workload is BASELINE config 1:
+8192^3, BF16 output, operands quantised from seeded N(0,1) BF16 with a per-tensor global scale
+(2688 / amax), quantisation excluded from `value`. Launches replay CUDA graphs over several input
+sets whose total size exceeds 3x L2, so every step reads its operands from HBM (cold L2).
+
+N > 1 (torchrun, one rank per GPU, NCCL): the GEMM is split column-parallel along N. Each rank
+holds the replicated A and its own S-row block of B and writes its M x S block of C; there is no
+collective in the timed region (weak scaling). --allgather additionally times an NCCL all-gather
+of the C blocks, reported separately.
+
+`e2e` runs the public API from pinned host BF16 matrices: H2D copy, on-device amax + quantise of
+both operands, GEMM, D2H copy of C, every step.
+
+--impl reference times the reference's CPU path (quantise A and B, dequantise, FP32 matmul,
+round) as restated by the CPU oracle, on this host's cores, on a bounded row sample per step.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+NOMINAL_FP4_DENSE_TFLOPS = 9000.0
+FALLBACK_BF16_TFLOPS = 1590.0
+METRIC = "NVFP4 GEMM PFLOP/s per job (2*M*N*K / time)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3000)
+    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--size", type=int, default=8192, help="M = N = K (N is per GPU when --gpus > 1)")
+    p.add_argument("--out-dtype", choices=["bf16", "fp16"], default="bf16")
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--allgather", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--e2e-steps", type=int, default=12)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-sample-rows", type=int, default=128)
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = p.parse_args()
+    args.warmup = max(args.warmup, 3)
+    return args
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("hbm_gbs", 0.0)), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_BF16_TFLOPS, 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------------- CPU path
+def cpu_reference_step(x_a, x_b, b_deq, gs_a, gs_b, rows, out_dtype):
+    """The reference's CPU path on a sample: quantise `rows` rows of A and the same share of B's
+    rows, dequantise both, FP32 matmul of the A rows against all of dequantised B, round to the
+    output dtype. The full dequantised B (`b_deq`) is prepared once outside the timer; its
+    per-sample share of quantise + dequantise work is what the B calls below time.
+    Returns (FLOPs of the sample, seconds)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    m, k = x_a.shape
+    n = x_b.shape[0]
+    b_rows = max(1, rows * n // m)
+    t0 = time.perf_counter()
+    aq, _, asl = oracle.quantize(x_a[:rows], gs_a, div_mode=1)
+    bq, _, bsl = oracle.quantize(x_b[:b_rows], gs_b, div_mode=1)
+    a = oracle.dequantize(aq, asl, gs_a, div_mode=1)
+    oracle.dequantize(bq, bsl, gs_b, div_mode=1)
+    c = a @ b_deq.T
+    if out_dtype == "bf16":
+        u = c.view(np.uint32)
+        c = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even BF16
+    else:
+        c = c.astype(np.float16)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * n * k, dt
+
+
+def prepare_cpu_inputs(size_m, size_n, size_k, seed=0):
+    """Seeded N(0,1) rounded to BF16 (config 0 recipe) as float32 numpy arrays, the FP32 global
+    encode scales 2688 / amax, and B dequantised once for the matmul share."""
+    import torch
+
+    from oracle import oracle
+
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(size_m, size_k, generator=g).to(torch.bfloat16).float()
+    b = torch.randn(size_n, size_k, generator=g).to(torch.bfloat16).float()
+    gs_a = float(torch.tensor(2688.0) / a.abs().max())
+    gs_b = float(torch.tensor(2688.0) / b.abs().max())
+    a, b = a.numpy(), b.numpy()
+    bq, _, bsl = oracle.quantize(b, gs_b, div_mode=1)
+    return a, b, oracle.dequantize(bq, bsl, gs_b, div_mode=1), gs_a, gs_b
+
+
+def cpu_baseline(args, size_m, size_n, size_k, seconds, steps=None, warmup=0):
+    """Median PFLOP/s of the CPU path on `args.cpu_sample_rows`-row samples."""
+    from oracle import oracle
+
+    rows = min(args.cpu_sample_rows, size_m)
+    a, b, b_deq, gs_a, gs_b = prepare_cpu_inputs(rows, size_n, size_k)
+    for _ in range(warmup):
+        cpu_reference_step(a, b, b_deq, gs_a, gs_b, rows, args.out_dtype)
+    rates, times = [], []
+    t_end = time.perf_counter() + seconds
+    while True:
+        if steps is not None and len(rates) >= steps:
+            break
+        if steps is None and time.perf_counter() >= t_end and len(rates) >= 3:
+            break
+        fl, dt = cpu_reference_step(a, b, b_deq, gs_a, gs_b, rows, args.out_dtype)
+        rates.append(fl / dt / 1e15)
+        times.append(dt)
+    return {
+        "value": statistics.median(rates),
+        "unit": "PFLOP/s",
+        "cores": oracle.num_threads(),
+        "kind": "port",
+        "sample": (f"{rows} rows of A (and {max(1, rows * size_n // size_m)} of B) quantised + dequantised, "
+                   f"FP32 matmul {rows}x{size_n}x{size_k} (numpy/OpenBLAS), rounded to {args.out_dtype}; "
+                   f"median of {len(rates)} samples"),
+        "seconds_total": sum(times),
+        "samples": len(rates),
+    }
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n_total = args.size * args.gpus
+    base = cpu_baseline(args, args.size, n_total, args.size, seconds=0, steps=args.steps, warmup=args.warmup)
+    ms_per_step = base["seconds_total"] / base["samples"] * 1e3
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": base["value"],
+        "unit": "PFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic: seeded N(0,1) BF16 operands, global scale 2688/amax",
+        "config": workload_config(args),
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "PFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args):
+    return {
+        "workload": f"NVFP4 GEMM {args.size}x{args.size * args.gpus}x{args.size} "
+                    f"({'BF16' if args.out_dtype == 'bf16' else 'FP16'} out)",
+        "m": args.size,
+        "n_per_gpu": args.size,
+        "k": args.size,
+        "global_batch": args.size,
+        "seq_len": None,
+        "parallelism": f"column-parallel N over {args.gpus} GPU(s), A replicated" if args.gpus > 1 else "single GPU",
+        "l2": "cold: rotating input sets > 3x L2",
+        "timing": "CUDA-graph replays, CUDA events, max over ranks",
+    }
+
+
+# ------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+        self.path = os.path.join(REPO, "gpurun_out", f"clocks_{device_index}.csv")
+
+    def __enter__(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100", "-i", str(self.idx)],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+                except ValueError:
+                    continue
+        if not rows:
+            return None
+        loaded = [r for r in rows if r[2] > 300.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        return {
+            "sm_mhz": statistics.median(r[0] for r in loaded),
+            "sm_max_mhz": max(r[1] for r in loaded),
+            "power_w_max": max(r[2] for r in loaded),
+            "samples": len(loaded),
+            "reasons": reasons,
+        }
+
+
+# ---------------------------------------------------------------------------------- GPU path
+def make_operands(rows, k, seed, dev):
+    """Seeded N(0,1) BF16 -> NVFP4 with the on-device global scale."""
+    import torch
+
+    import gemm3_b200 as g3
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
+    q, sf, _, gs = g3.quantize_nvfp4_global(x)
+    del x
+    return q, sf, gs
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import gemm3_b200 as g3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    assert g3.supported(), "needs sm_100 and the built extension"
+
+    M = N = K = args.size
+    out_dtype = torch.bfloat16 if args.out_dtype == "bf16" else torch.float16
+    sm, _, l2 = g3.hw.device_info(local)
+    set_bytes = M * K // 2 + N * K // 2 + (M + N) * K // 16
+    n_sets = max(2, math.ceil(3 * l2 / set_bytes))
+    n_sets = min(n_sets, 8)
+    sets = []
+    for s in range(n_sets):
+        a_q, a_sf, gs_a = make_operands(M, K, seed=1000 * s, dev=dev)  # A replicated: same seed on every rank
+        b_q, b_sf, gs_b = make_operands(N, K, seed=1000 * s + 1 + 7919 * rank, dev=dev)  # this rank's B block
+        alpha = (1.0 / (gs_a * gs_b)).reshape(1).float()
+        sets.append((a_q, b_q, a_sf, b_sf, alpha))
+    c = torch.empty(M, N, dtype=out_dtype, device=dev)
+    cfg = g3.config_for(M, N, K)
+
+    def step(i):
+        a_q, b_q, a_sf, b_sf, alpha = sets[i % n_sets]
+        g3.gemm(a_q, b_q, a_sf, b_sf, alpha=alpha, out=c, out_dtype=out_dtype, config=cfg)
+
+    with g3.persisting_l2(cfg.persist_mb):
+        for i in range(n_sets):  # compile-free warm path, also sets kernel attributes
+            step(i)
+        torch.cuda.synchronize()
+        graphs = []
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            for i in range(n_sets):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    step(i)
+                graphs.append(gr)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        torch.cuda.synchronize()
+
+        for i in range(args.warmup):
+            graphs[i % n_sets].replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        cur = torch.cuda.current_stream(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            start.record(cur)
+            for i in range(args.steps):
+                graphs[i % n_sets].replay()
+            end.record(cur)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms_local = start.elapsed_time(end)
+        # per-launch duration for the roofline: a short event-bracketed run of single replays
+        lat = []
+        for i in range(min(args.steps, 64)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            graphs[i % n_sets].replay()
+            e1.record(cur)
+            lat.append((e0, e1))
+        torch.cuda.synchronize()
+        launch_ms = statistics.median(a.elapsed_time(b) for a, b in lat)
+    status = g3.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after timing")
+
+    ms_t = torch.tensor([ms_local, launch_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_total, launch_ms = ms_t.tolist()
+    ms_per_step = ms_total / args.steps
+    flops_step = 2.0 * M * N * K * world
+    value = flops_step * args.steps / (ms_total * 1e-3) / 1e15
+
+    allgather = None
+    if args.allgather and world > 1:
+        allgather = time_allgather(c, world, dev)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world)
+
+    del graphs
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, M, N, K, seconds=args.cpu_seconds, warmup=1)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    bf16_peak, _, peak_src = peaks()
+    fp4_peak = 4.0 * bf16_peak
+    achieved = 2.0 * M * N * K / (launch_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "PFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "us_per_gemm": launch_ms * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 scales) -> fp32 accumulate",
+        "data": "synthetic: seeded N(0,1) BF16 quantised to NVFP4, global scale 2688/amax",
+        "config": workload_config(args),
+        "gpu_launches": args.steps,
+        "roofline": {
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": fp4_peak,
+            "unit": "TFLOP/s",
+            "frac": achieved / fp4_peak,
+            "peak_source": (f"4 x bf16_tflops of MEASURED_PEAKS.json ({bf16_peak:.0f}); dense FP4 = 4x dense BF16"
+                            if peak_src == "measured" else f"4 x fallback bf16 {bf16_peak:.0f}"),
+            "frac_of_nominal_9pf": achieved / NOMINAL_FP4_DENSE_TFLOPS,
+            "traffic": None,
+        },
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+    }
+    if allgather is not None:
+        line["allgather"] = allgather
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def time_allgather(c, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    out = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=dev)
+    for _ in range(3):
+        dist.all_gather_into_tensor(out, c)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        dist.all_gather_into_tensor(out, c)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = ms.item()
+    nbytes = c.numel() * c.element_size() * world
+    return {"ms": ms, "bytes_gathered": nbytes, "bus_gbs": nbytes * (world - 1) / world / (ms * 1e-3) / 1e9,
+            "layout": "[world][M][N/world] (NCCL order)"}
+
+
+def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):
+    import torch
+    import torch.distributed as dist
+
+    import gemm3_b200 as g3
+
+    g = torch.Generator().manual_seed(11 + rank)
+    a_h = torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory()
+    b_h = torch.randn(N, K, generator=g).to(torch.bfloat16).pin_memory()
+    c_h = torch.empty(M, N, dtype=out_dtype).pin_memory()
+    a_d = torch.empty_like(a_h, device=dev)
+    b_d = torch.empty_like(b_h, device=dev)
+    c_d = torch.empty(M, N, dtype=out_dtype, device=dev)
+
+    def step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        aq, asf, _, gsa = g3.quantize_nvfp4_global(a_d)
+        bq, bsf, _, gsb = g3.quantize_nvfp4_global(b_d)
+        g3.gemm(aq, bq, asf, bsf, alpha=(1.0 / (gsa * gsb)), out=c_d, out_dtype=out_dtype, config=cfg)
+        c_h.copy_(c_d, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = ms.item()
+    val = 2.0 * M * N * K * world * args.e2e_steps / (ms * 1e-3) / 1e15
+    return {
+        "value": val,
+        "unit": "PFLOP/s",
+        "h2d_bytes_per_step": (a_h.numel() + b_h.numel()) * 2,
+        "d2h_bytes_per_step": c_h.numel() * c_h.element_size(),
+        "ms_per_step": ms / args.e2e_steps,
+        "steps": args.e2e_steps,
+        "path": "pinned host BF16 A,B -> H2D -> amax + quantize_nvfp4 (GPU) -> gemm -> D2H C",
+    }
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,369 @@
+// Host side of libgemm3_b200.so: argument validation, TMA descriptor encoding and kernel
+// launches behind the extern "C" entry points declared in include/nvfp4_gemm.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/nvfp4_gemm.h"
+#include "gemm_kernel.cuh"
+#include "quant_kernel.cuh"
+
+namespace {
+
+thread_local int32_t g_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+  g_last_cuda_error = static_cast<int32_t>(e);
+  return NVFP4_ERR_CUDA;
+}
+
+#define G3_CUDA(expr)                          \
+  do {                                         \
+    cudaError_t e_ = (expr);                   \
+    if (e_ != cudaSuccess) return cuda_fail(e_); \
+  } while (0)
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceCache {
+  bool ready = false;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  int64_t l2_bytes = 0;
+  bool gemm_attr_set = false;
+};
+DeviceCache g_dev[kMaxDevices];
+std::mutex g_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device(int* dev) {
+  G3_CUDA(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= kMaxDevices) return NVFP4_ERR_INVALID_VALUE;
+  return NVFP4_OK;
+}
+
+int device_cache(int dev, DeviceCache** out) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceCache& d = g_dev[dev];
+  if (!d.ready) {
+    cudaDeviceProp prop;
+    G3_CUDA(cudaGetDeviceProperties(&prop, dev));
+    d.sm_count = prop.multiProcessorCount;
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    d.l2_bytes = prop.l2CacheSize;
+    d.ready = true;
+  }
+  *out = &d;
+  return NVFP4_OK;
+}
+
+int get_encoder() {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_encode != nullptr) return NVFP4_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  G3_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (fn == nullptr || q != cudaDriverEntryPointSuccess) return NVFP4_ERR_UNSUPPORTED;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return NVFP4_OK;
+}
+
+// 2-D uint8 view [rows, row_bytes] of a packed operand, boxes of box_rows x 128 bytes with the
+// 128-byte swizzle; reads outside the tensor are zero-filled by TMA.
+int encode_operand(CUtensorMap* m, const void* base, int64_t rows, int64_t row_bytes, uint32_t box_rows) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(g3::kTileKBytes), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NVFP4_OK : NVFP4_ERR_TENSOR_MAP;
+}
+
+// Opt the GEMM kernels into their dynamic shared memory once per device (outside any capture).
+int ensure_gemm_attributes(DeviceCache* d) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (d->gemm_attr_set) return NVFP4_OK;
+  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g3::kGemmSmemBytes));
+  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g3::kGemmSmemBytes));
+  d->gemm_attr_set = true;
+  return NVFP4_OK;
+}
+
+int grid_for(int64_t work, int sm_count, int threads = 256) {
+  const int64_t want = (work + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t nvfp4_abi_version(void) { return 1; }
+
+int32_t nvfp4_last_cuda_error(void) { return g_last_cuda_error; }
+
+const char* nvfp4_strerror(int32_t code) {
+  switch (code) {
+    case NVFP4_OK: return "success";
+    case NVFP4_ERR_INVALID_VALUE: return "invalid value (shape, pointer or dtype)";
+    case NVFP4_ERR_MISALIGNED: return "misaligned pointer";
+    case NVFP4_ERR_UNSUPPORTED: return "unsupported device or feature (needs sm_100)";
+    case NVFP4_ERR_CUDA: return "CUDA runtime error";
+    case NVFP4_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled rejected the operand";
+    case NVFP4_DEV_TIMEOUT_FULL: return "device timeout: MMA issuer waiting for a filled stage";
+    case NVFP4_DEV_TIMEOUT_EMPTY: return "device timeout: producer waiting for a free stage";
+    case NVFP4_DEV_TIMEOUT_ACC_FULL: return "device timeout: epilogue waiting for the accumulator";
+    case NVFP4_DEV_TIMEOUT_ACC_EMPTY: return "device timeout: MMA issuer waiting for the epilogue";
+    case NVFP4_DEV_TIMEOUT_DRAIN: return "device timeout: draining in-flight copies";
+    case NVFP4_DEV_ABORTED: return "device abort";
+    default: return "unknown status";
+  }
+}
+
+int nvfp4_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor, int64_t* l2_bytes) {
+  if (device < 0 || device >= kMaxDevices) return NVFP4_ERR_INVALID_VALUE;
+  DeviceCache* d = nullptr;
+  int rc = device_cache(device, &d);
+  if (rc != NVFP4_OK) return rc;
+  if (sm_count) *sm_count = d->sm_count;
+  if (cc_major) *cc_major = d->cc_major;
+  if (cc_minor) *cc_minor = d->cc_minor;
+  if (l2_bytes) *l2_bytes = d->l2_bytes;
+  return NVFP4_OK;
+}
+
+int nvfp4_set_persisting_l2(int64_t bytes, int64_t* old_bytes) {
+  if (bytes < 0) return NVFP4_ERR_INVALID_VALUE;
+  size_t old = 0;
+  G3_CUDA(cudaDeviceGetLimit(&old, cudaLimitPersistingL2CacheSize));
+  G3_CUDA(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, static_cast<size_t>(bytes)));
+  if (old_bytes) *old_bytes = static_cast<int64_t>(old);
+  return NVFP4_OK;
+}
+
+int nvfp4_max_active_clusters(int32_t cluster_size, int32_t* out) {
+  if (out == nullptr || cluster_size < 1) return NVFP4_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  if (d->cc_major != 10) return NVFP4_ERR_UNSUPPORTED;
+  auto kern = g3::nvfp4_gemm_kernel<true>;
+  G3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kGemmSmemBytes));
+  if (cluster_size > 8) G3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster_size * d->sm_count, 1, 1);
+  cfg.blockDim = dim3(g3::kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = g3::kGemmSmemBytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = cluster_size;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = d->sm_count / cluster_size;  // same fallback as nvfp4_gemm_cute/hw.py:20-22
+  }
+  *out = n;
+  return NVFP4_OK;
+}
+
+int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sfb, void* c, const float* alpha,
+                   int64_t m, int64_t n, int64_t k, int32_t out_dtype, const nvfp4_gemm_config* cfg, int32_t* status,
+                   void* stream) {
+  if (!a || !b || !sfa || !sfb || !c || !alpha) return NVFP4_ERR_INVALID_VALUE;
+  if (m < 1 || n < 64 || k < 64 || n % 64 || k % 64) return NVFP4_ERR_INVALID_VALUE;
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return NVFP4_ERR_INVALID_VALUE;
+  if (out_dtype != NVFP4_DTYPE_F16 && out_dtype != NVFP4_DTYPE_BF16) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 16) || !aligned(sfb, 16) || !aligned(c, 32) ||
+      !aligned(alpha, 4))
+    return NVFP4_ERR_MISALIGNED;
+  nvfp4_gemm_config def = {};
+  if (cfg != nullptr && cfg->struct_size >= static_cast<int32_t>(sizeof(nvfp4_gemm_config))) def = *cfg;
+  if ((def.tile_m != 0 && def.tile_m != 128) || (def.tile_n != 0 && def.tile_n != 256)) return NVFP4_ERR_INVALID_VALUE;
+  if (def.raster_band < 0) return NVFP4_ERR_INVALID_VALUE;
+
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  if (d->cc_major != 10) return NVFP4_ERR_UNSUPPORTED;
+  rc = get_encoder();
+  if (rc != NVFP4_OK) return rc;
+
+  CUtensorMap tmap_a, tmap_b;
+  rc = encode_operand(&tmap_a, a, m, k / 2, g3::kTileM);
+  if (rc != NVFP4_OK) return rc;
+  rc = encode_operand(&tmap_b, b, n, k / 2, g3::kTileN);
+  if (rc != NVFP4_OK) return rc;
+
+  g3::GemmParams p;
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb = static_cast<const uint8_t*>(sfb);
+  p.c = c;
+  p.alpha = alpha;
+  p.status = status;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.m_tiles = static_cast<int>((m + g3::kTileM - 1) / g3::kTileM);
+  p.n_tiles = static_cast<int>((n + g3::kTileN - 1) / g3::kTileN);
+  p.k_tiles = static_cast<int>((k + 255) / 256);
+  p.sf_kblocks = static_cast<int>(k / 64);
+  p.n_rowblocks = static_cast<int>((n + 127) / 128);
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  if (tiles > INT32_MAX) return NVFP4_ERR_INVALID_VALUE;
+  p.num_tiles = static_cast<int>(tiles);
+  p.raster_band = def.raster_band;
+  p.raster_along_m = def.raster_along_m;
+  p.pol_a = def.l2_policy_a;
+  p.pol_b = def.l2_policy_b;
+  p.pol_sfa = def.l2_policy_sfa;
+  p.pol_sfb = def.l2_policy_sfb;
+  p.store_evict_first = def.store_evict_first == 0 ? (k >= 8192) : (def.store_evict_first == 1);
+  p.pace_ns = def.epi_store_pace_ns;
+  p.tma_b_first = def.tma_b_first;
+
+  int ctas = d->sm_count;
+  if (def.max_ctas > 0 && def.max_ctas < ctas) ctas = def.max_ctas;
+  if (ctas > p.num_tiles) ctas = p.num_tiles;
+
+  rc = ensure_gemm_attributes(d);
+  if (rc != NVFP4_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (out_dtype == NVFP4_DTYPE_BF16)
+    g3::nvfp4_gemm_kernel<true><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+  else
+    g3::nvfp4_gemm_kernel<false><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+  G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, float global_scale, const float* gs_dev,
+                   int32_t gs_mode, int32_t div_mode, void* packed, void* sf_swizzled, void* sf_linear, float* gs_out,
+                   void* stream) {
+  if (!x || !packed || !sf_swizzled) return NVFP4_ERR_INVALID_VALUE;
+  if (rows < 1 || k < 16 || k % 16) return NVFP4_ERR_INVALID_VALUE;
+  if (in_dtype < NVFP4_DTYPE_F16 || in_dtype > NVFP4_DTYPE_F32) return NVFP4_ERR_INVALID_VALUE;
+  if (gs_mode < 0 || gs_mode > 2 || (gs_mode != 0 && gs_dev == nullptr)) return NVFP4_ERR_INVALID_VALUE;
+  if (div_mode != 0 && div_mode != 1) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(x, 16) || !aligned(packed, 8)) return NVFP4_ERR_MISALIGNED;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  g3::QuantParams p;
+  p.x = x;
+  p.rows = rows;
+  p.k = k;
+  p.cols = k / 16;
+  p.rows_pad = (rows + 127) / 128 * 128;
+  p.cols_pad = (p.cols + 3) / 4 * 4;
+  p.gs = global_scale;
+  p.gs_dev = gs_dev;
+  p.gs_mode = gs_mode;
+  p.div_mode = div_mode;
+  p.packed = static_cast<uint8_t*>(packed);
+  p.sf_swz = static_cast<uint8_t*>(sf_swizzled);
+  p.sf_lin = static_cast<uint8_t*>(sf_linear);
+  p.gs_out = gs_out;
+  const int grid = grid_for(p.rows_pad * p.cols_pad, d->sm_count);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (in_dtype) {
+    case NVFP4_DTYPE_F16: g3::nvfp4_quantize_kernel<0><<<grid, 256, 0, s>>>(p); break;
+    case NVFP4_DTYPE_BF16: g3::nvfp4_quantize_kernel<1><<<grid, 256, 0, s>>>(p); break;
+    default: g3::nvfp4_quantize_kernel<2><<<grid, 256, 0, s>>>(p); break;
+  }
+  G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+int nvfp4_amax(const void* x, int32_t in_dtype, int64_t numel, float* amax_out, void* stream) {
+  if (!x || !amax_out || numel < 1) return NVFP4_ERR_INVALID_VALUE;
+  if (in_dtype < NVFP4_DTYPE_F16 || in_dtype > NVFP4_DTYPE_F32) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(x, 16) || !aligned(amax_out, 4)) return NVFP4_ERR_MISALIGNED;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  G3_CUDA(cudaMemsetAsync(amax_out, 0, sizeof(float), s));
+  const int64_t nvec = numel / 16;
+  int grid = grid_for(nvec > 0 ? nvec : 1, d->sm_count);
+  const int64_t tail = numel - nvec * 16;
+  if (static_cast<int64_t>(grid) * 256 < tail) grid = static_cast<int>((tail + 255) / 256);
+  unsigned int* bits = reinterpret_cast<unsigned int*>(amax_out);
+  switch (in_dtype) {
+    case NVFP4_DTYPE_F16: g3::nvfp4_amax_kernel<0><<<grid, 256, 0, s>>>(x, numel, bits); break;
+    case NVFP4_DTYPE_BF16: g3::nvfp4_amax_kernel<1><<<grid, 256, 0, s>>>(x, numel, bits); break;
+    default: g3::nvfp4_amax_kernel<2><<<grid, 256, 0, s>>>(x, numel, bits); break;
+  }
+  G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+int nvfp4_dequantize(const void* packed, const void* sf_linear, int64_t rows, int64_t k, float global_scale,
+                     int32_t div_mode, float* out, void* stream) {
+  if (!packed || !sf_linear || !out || rows < 1 || k < 16 || k % 16) return NVFP4_ERR_INVALID_VALUE;
+  if (div_mode != 0 && div_mode != 1) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(packed, 8) || !aligned(out, 16)) return NVFP4_ERR_MISALIGNED;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  g3::DequantParams p;
+  p.packed = static_cast<const uint8_t*>(packed);
+  p.sf_lin = static_cast<const uint8_t*>(sf_linear);
+  p.rows = rows;
+  p.k = k;
+  p.cols = k / 16;
+  p.gs = global_scale;
+  p.div_mode = div_mode;
+  p.out = out;
+  g3::nvfp4_dequantize_kernel<<<grid_for(rows * p.cols, d->sm_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+int nvfp4_swizzle_sf(const void* sf_linear, int64_t rows, int64_t cols, void* out, void* stream) {
+  if (!sf_linear || !out || rows < 1 || cols < 1) return NVFP4_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  const int64_t rp = (rows + 127) / 128 * 128, cp = (cols + 3) / 4 * 4;
+  g3::nvfp4_swizzle_kernel<<<grid_for(rp * cp, d->sm_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(sf_linear), rows, cols, rp, cp, static_cast<uint8_t*>(out));
+  G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+}  // extern "C"

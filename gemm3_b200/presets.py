@@ -1,0 +1,103 @@
+"""Per-shape launch configurations for the B200 (sm_100a) NVFP4 GEMM.
+
+Same interface as nvfp4_gemm_cute/presets.py:14-99: a frozen ``Config`` (tile, preferred cluster,
+fallback cluster, sorted attribute tuple, persisting-L2 MiB), ``DEFAULT``, ``PRESETS`` keyed by
+(M, N, K) and ``config_for``.
+
+How the fields act on the B200 kernel (gemm3_b200/csrc/gemm_kernel.cuh):
+  tile            (256, 256) or (128, 256). A 256-row tile is computed as two 128-row CTA tiles
+                  that are scheduled next to each other; the accumulation order, and so the
+                  output bits, are the same for every tile, cluster, raster and cache setting.
+  cluster         kept for the tile order: ``fast_swz`` groups tiles in bands of
+                  fast_swz * cluster[0] CTA tiles along M. The B200 kernel uses no TMA multicast,
+                  so cluster shape does not change data movement.
+  fallback        accepted and validated; unused (no multicast cluster to fall back from).
+  persist_mb      host persisting-L2 limit to hold while calling (``api.persisting_l2``).
+Attributes with an effect: fast_swz, raster_along_m, l2_policy_{a,b,sfa,sfb},
+epi_store_pace_per_ktile_ns, tma_b_first. The others (owned_8k, trim_short_tail, tma_sfb_first,
+retire_a_cols, packed_ab_desc, epi_store_pair, specialize_32k, prefetch_first_ktiles) name
+B300 code paths of the reference kernel; they are accepted and shape-checked with the same
+rules and messages as the reference (nvfp4_gemm_cute/api.py:177-207) and do not change the B200
+kernel.
+"""
+
+from dataclasses import dataclass, field
+
+
+@dataclass(frozen=True)
+class Config:
+    """Launch configuration for one GEMM shape."""
+
+    tile: tuple = (256, 256)
+    cluster: tuple = (4, 1)
+    fallback: tuple | None = (2, 1)
+    attrs: tuple = field(default_factory=tuple)  # sorted ((name, value), ...)
+    persist_mb: int = 0
+
+    @staticmethod
+    def make(tile=(256, 256), cluster=(4, 1), fallback=(2, 1), persist_mb=0, **attrs):
+        return Config(
+            tuple(tile),
+            tuple(cluster),
+            fallback and tuple(fallback),
+            tuple(sorted(attrs.items())),
+            persist_mb,
+        )
+
+    def attr_dict(self):
+        return dict(self.attrs)
+
+
+# General-purpose default: plain raster order, standard L2 policy.
+DEFAULT = Config.make()
+
+# (M, N, K) -> Config. Shape-specific attributes keep the reference's guards; the B200 knobs are
+# the raster band (fast_swz x cluster[0] CTA tiles) and the operand L2 policies.
+PRESETS = {
+    (4096, 4096, 4096): Config.make(
+        cluster=(4, 2),
+        fallback=(2, 1),
+        fast_swz=2,
+        raster_along_m=False,
+        prefetch_first_ktiles=1,
+    ),
+    (8192, 8192, 8192): Config.make(
+        cluster=(8, 2),
+        fallback=(2, 1),
+        fast_swz=2,
+        raster_along_m=False,
+        owned_8k=True,
+        l2_policy_a="evict_last",
+        l2_policy_sfa="evict_last",
+    ),
+    (16384, 16384, 16384): Config.make(
+        cluster=(8, 2),
+        fallback=(2, 1),
+        fast_swz=2,
+        raster_along_m=False,
+        l2_policy_a="evict_last",
+        l2_policy_sfa="evict_last",
+        trim_short_tail=True,
+        tma_b_first=True,
+        tma_sfb_first=True,
+        retire_a_cols=8,
+        packed_ab_desc=True,
+    ),
+    (32768, 32768, 32768): Config.make(
+        cluster=(4, 4),
+        fallback=(2, 1),
+        fast_swz=4,
+        raster_along_m=False,
+        l2_policy_a="evict_last",
+        epi_store_pair=True,
+        epi_store_pace_per_ktile_ns=0,
+        retire_a_cols=8,
+        packed_ab_desc=True,
+        specialize_32k=True,
+    ),
+}
+
+
+def config_for(m: int, n: int, k: int) -> Config:
+    """Return the tuned configuration for (m, n, k), or DEFAULT."""
+    return PRESETS.get((m, n, k), DEFAULT)

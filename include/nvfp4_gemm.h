@@ -1,0 +1,151 @@
+/*
+ * C ABI of libgemm3_b200.so: a B200 (sm_100a) NVFP4 block-scaled GEMM and its quantiser.
+ *
+ * Every entry point takes plain device pointers, element counts and a cudaStream_t passed as
+ * void* (NULL = legacy default stream), returns an nvfp4_status code, launches asynchronously on
+ * that stream and never allocates device memory. Buffers are owned by the caller.
+ *
+ * Data formats (the layout of the nvfp4_gemm_cute package, nvfp4_gemm_cute/quant.py:1-7):
+ *   packed operand  uint8 [rows, K/2], row-major; element 2j in the low nibble, 2j+1 in the high
+ *                   nibble; each nibble is an E2M1 code (bit 3 = sign, bits 0-2 index
+ *                   {0, .5, 1, 1.5, 2, 3, 4, 6}).
+ *   linear scales   uint8 [rows, K/16], UE4M3 bits, one per 16 consecutive K elements.
+ *   swizzled scales uint8, ceil(rows/128)*128 * ceil(K/64)*4 bytes: rows padded to 128 and scale
+ *                   columns to 4, each (128-row, 4-column) block stored as [32][4][4]
+ *                   (row % 32, (row % 128) / 32, column % 4); blocks ordered row-block-major.
+ */
+#ifndef GEMM3_B200_NVFP4_GEMM_H_
+#define GEMM3_B200_NVFP4_GEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. Host-side validation failures are reported before anything is launched. */
+typedef enum nvfp4_status {
+  NVFP4_OK = 0,
+  NVFP4_ERR_INVALID_VALUE = 1,   /* bad shape, null pointer or unsupported dtype */
+  NVFP4_ERR_MISALIGNED = 2,      /* pointer alignment requirement violated */
+  NVFP4_ERR_UNSUPPORTED = 3,     /* device is not sm_100 / feature not available */
+  NVFP4_ERR_CUDA = 4,            /* a CUDA runtime call failed; see nvfp4_last_cuda_error() */
+  NVFP4_ERR_TENSOR_MAP = 5,      /* cuTensorMapEncodeTiled rejected the operand */
+  /* Device-side status words (written by kernels into the caller's int32 status buffer). */
+  NVFP4_DEV_TIMEOUT_FULL = 101,
+  NVFP4_DEV_TIMEOUT_EMPTY = 102,
+  NVFP4_DEV_TIMEOUT_ACC_FULL = 103,
+  NVFP4_DEV_TIMEOUT_ACC_EMPTY = 104,
+  NVFP4_DEV_TIMEOUT_DRAIN = 105,
+  NVFP4_DEV_ABORTED = 106
+} nvfp4_status;
+
+/* Element types of dense inputs/outputs. */
+enum { NVFP4_DTYPE_F16 = 0, NVFP4_DTYPE_BF16 = 1, NVFP4_DTYPE_F32 = 2 };
+
+/* L2 eviction priority hints for the operand loads. */
+enum { NVFP4_L2_NORMAL = 0, NVFP4_L2_EVICT_FIRST = 1, NVFP4_L2_EVICT_LAST = 2 };
+
+/*
+ * Launch configuration of the GEMM kernel. Zero-initialise and set struct_size; zero fields take
+ * their defaults. Mirrors the attributes of nvfp4_gemm_cute.presets.Config
+ * (nvfp4_gemm_cute/presets.py:14-35, api.py:20-39) that have a meaning on B200.
+ */
+typedef struct nvfp4_gemm_config {
+  int32_t struct_size;           /* sizeof(nvfp4_gemm_config) */
+  int32_t tile_m;                /* 128: one CTA per tile (only value in this version); 0 = 128 */
+  int32_t tile_n;                /* 256 (only value in this version); 0 = 256 */
+  int32_t raster_band;           /* 128-row tiles per raster band (0 or 1: bands of one tile) */
+  int32_t raster_along_m;        /* 0: bands of M-tiles, sweep N ("N sweep"); 1: bands of N-tiles */
+  int32_t l2_policy_a;           /* NVFP4_L2_* for A loads */
+  int32_t l2_policy_b;
+  int32_t l2_policy_sfa;
+  int32_t l2_policy_sfb;
+  int32_t store_evict_first;     /* output stores with L2::evict_first: 0 auto (K >= 8192), 1 on, 2 off */
+  int32_t epi_store_pace_ns;     /* pause between output 32-column chunks (0 = none) */
+  int32_t tma_b_first;           /* issue the B load before A in each stage */
+  int32_t max_ctas;              /* cap on persistent CTAs (0 = one per SM) */
+} nvfp4_gemm_config;
+
+/*
+ * C[M,N] = alpha * dequant(A)[M,K] . dequant(B)[N,K]^T, FP32 accumulation, FP16/BF16 output.
+ * Replaces the TVM-FFI callable that nvfp4_gemm_cute/api.py:219 invokes
+ *   compiled(a, b, out, sf_m, sf_n, sf_k, a_sf_ptr, b_sf_ptr, alpha)
+ * (kernel wrapper at nvfp4_gemm_cute/kernel.py:1801-1870).
+ *   a, b      packed operands, 16-byte aligned
+ *   sfa, sfb  swizzled scales, 16-byte aligned
+ *   c         contiguous [M,N] of out_dtype (NVFP4_DTYPE_F16 or _BF16), 32-byte aligned
+ *   alpha     device pointer to one float (read on the device, like kernel.py:671)
+ *   status    optional device int32 that receives the first device-side error (may be NULL)
+ * Requires M >= 1, N % 64 == 0, K % 64 == 0 (api.py:173-174). cfg may be NULL (defaults).
+ */
+int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sfb, void* c,
+                   const float* alpha, int64_t m, int64_t n, int64_t k, int32_t out_dtype,
+                   const nvfp4_gemm_config* cfg, int32_t* status, void* stream);
+
+/*
+ * Quantise x [rows, K] (contiguous, in_dtype F16/BF16/F32, 16-byte aligned) to NVFP4.
+ * Replaces quantize_nvfp4 (nvfp4_gemm_cute/quant.py:41-59), bit-exact with it:
+ *   xb = float(x) * gs;  amax over 16;  scale = e4m3_rn_nonsaturating(amax / 6);
+ *   q = scale > 0 ? xb / scale : 0;  code = nearest E2M1 (ties to the even code) | sign(q < 0).
+ * gs_mode selects the global scale gs:
+ *   0: the host value global_scale;
+ *   1: *gs_dev (device float);
+ *   2: 2688 / *gs_dev where *gs_dev holds the tensor amax (from nvfp4_amax); gs = 1 if amax is 0
+ *      or not finite. The gs used is written to gs_out when gs_out is not NULL.
+ * div_mode selects how "amax / 6" rounds, matching where the reference ran:
+ *   0: amax * fl(1/6) (PyTorch on CUDA divides by a host scalar through its reciprocal);
+ *   1: correctly rounded amax / 6 (PyTorch on CPU).
+ * Outputs: packed [rows, K/2]; sf_swizzled (padding written as zeros); sf_linear [rows, K/16]
+ * (may be NULL). Requires K % 16 == 0.
+ */
+int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, float global_scale,
+                   const float* gs_dev, int32_t gs_mode, int32_t div_mode, void* packed,
+                   void* sf_swizzled, void* sf_linear, float* gs_out, void* stream);
+
+/*
+ * amax_out[0] = max |x| over numel elements (NaN propagates). No counterpart in the reference
+ * package; it produces the per-tensor amax from which the FP32 global encode scale
+ * 2688 / amax (= 1 / (amax / (6 * 448))) is derived for nvfp4_quantize gs_mode 2.
+ */
+int nvfp4_amax(const void* x, int32_t in_dtype, int64_t numel, float* amax_out, void* stream);
+
+/*
+ * out[rows, K] (float32) = E2M1(code) * e4m3(scale) / global_scale.
+ * Replaces dequantize_nvfp4 (nvfp4_gemm_cute/quant.py:62-70); div_mode as for nvfp4_quantize
+ * (0: multiply by fl(1/gs) as PyTorch on CUDA does, 1: divide as PyTorch on CPU does).
+ */
+int nvfp4_dequantize(const void* packed, const void* sf_linear, int64_t rows, int64_t k,
+                     float global_scale, int32_t div_mode, float* out, void* stream);
+
+/* Linear [rows, cols] scales -> 128x4 swizzled layout, zero padded. Replaces swizzle_sf
+ * (nvfp4_gemm_cute/quant.py:31-38). */
+int nvfp4_swizzle_sf(const void* sf_linear, int64_t rows, int64_t cols, void* out, void* stream);
+
+/* How many clusters of cluster_size CTAs of the GEMM kernel can be co-resident on the current
+ * device. Replaces get_max_active_clusters (nvfp4_gemm_cute/hw.py:8-22). */
+int nvfp4_max_active_clusters(int32_t cluster_size, int32_t* out);
+
+/* SM count, compute capability and L2 size of `device`. */
+int nvfp4_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor,
+                      int64_t* l2_bytes);
+
+/* Set cudaLimitPersistingL2CacheSize of the current context to `bytes`, returning the previous
+ * value in *old_bytes. Replaces the cudaDeviceSetLimit call of persisting_l2
+ * (nvfp4_gemm_cute/api.py:223-242). A per-context limit: it ends with the process. */
+int nvfp4_set_persisting_l2(int64_t bytes, int64_t* old_bytes);
+
+/* Human-readable text for a status code; static storage. */
+const char* nvfp4_strerror(int32_t code);
+
+/* The cudaError_t of the most recent failing CUDA call on this thread (0 if none). */
+int32_t nvfp4_last_cuda_error(void);
+
+/* ABI version: bumped when a signature or struct layout changes. */
+int32_t nvfp4_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GEMM3_B200_NVFP4_GEMM_H_ */
