@@ -33,8 +33,13 @@ constexpr int kSfaBytes = kKBlocksPerTile * kSfChunk;       // 2 KiB
 constexpr int kSfbBytes = 2 * kKBlocksPerTile * kSfChunk;   // 4 KiB
 constexpr int kTmemCols = 512;
 constexpr int kAccCol = 0;
-constexpr int kSfaCol = 256;  // 4 columns per 64-element block
-constexpr int kSfbCol = 272;  // 8 columns per 64-element block (two 128-row halves)
+// Scale factors get one TMEM region per shared-memory stage, so the copies for k-tile t+1 never
+// overwrite columns that the MMAs of k-tile t are still reading (that hazard drains the tensor
+// pipe once per k-tile). Per stage: SFA 4 columns per 64-element block, SFB 8 (two 128-row halves).
+constexpr int kSfColsPerStage = 4 * kKBlocksPerTile + 8 * kKBlocksPerTile;  // 48
+constexpr int kSfaCol = 256;
+constexpr int kSfbCol = kSfaCol + 4 * kKBlocksPerTile;
+static_assert(kSfaCol + kStages * kSfColsPerStage <= kTmemCols, "scale factors do not fit in TMEM");
 constexpr int kGemmThreads = 192;
 
 constexpr int kOffA = 0;
@@ -241,15 +246,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t sb = smem_u32(smem + kOffB + stage * kBBytes);
           const uint32_t ssfa = smem_u32(smem + kOffSfa + stage * kSfaBytes);
           const uint32_t ssfb = smem_u32(smem + kOffSfb + stage * kSfbBytes);
-          for (int j = 0; j < nkb; ++j)
-            tc_cp_32x128b_warpx4(tmem + kSfaCol + 4 * j, sdesc_sf_chunk(ssfa + j * kSfChunk));
-          for (int rb = 0; rb < nrb; ++rb)
-            for (int j = 0; j < nkb; ++j)
-              tc_cp_32x128b_warpx4(tmem + kSfbCol + 8 * j + 4 * rb,
-                                   sdesc_sf_chunk(ssfb + rb * (kKBlocksPerTile * kSfChunk) + j * kSfChunk));
-          for (int j = 0; j < nkb; ++j) {
-            tc_mma_nvf4(tmem + kAccCol, sdesc_kmajor_sw128(sa + 32 * j), sdesc_kmajor_sw128(sb + 32 * j), idesc,
-                        tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, (kt | j) != 0 ? 1u : 0u);
+          const uint32_t tsfa = tmem + kSfaCol + stage * kSfColsPerStage;
+          const uint32_t tsfb = tmem + kSfbCol + stage * kSfColsPerStage;
+          if (nkb == kKBlocksPerTile && nrb == 2) {
+            // Full k-tile: straight-line issue, scale copies interleaved with the MMA that reads
+            // them. Runtime-bounded loops between tcgen05 instructions cost ~70% more issue time.
+            const uint64_t da = sdesc_kmajor_sw128(sa), db = sdesc_kmajor_sw128(sb);
+            const uint64_t dsa = sdesc_sf_chunk(ssfa), dsb = sdesc_sf_chunk(ssfb);
+#pragma unroll
+            for (int j = 0; j < kKBlocksPerTile; ++j) {
+              // descriptor start addresses are in 16-byte units: +32 B per K=64 step, +512 B per chunk
+              tc_cp_32x128b_warpx4(tsfa + 4 * j, dsa + 32 * j);
+              tc_cp_32x128b_warpx4(tsfb + 8 * j, dsb + 32 * j);
+              tc_cp_32x128b_warpx4(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+              tc_mma_nvf4(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
+                          (kt | j) != 0 ? 1u : 0u);
+            }
+          } else {
+            for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4(tsfa + 4 * j, sdesc_sf_chunk(ssfa + j * kSfChunk));
+            for (int rb = 0; rb < nrb; ++rb)
+              for (int j = 0; j < nkb; ++j)
+                tc_cp_32x128b_warpx4(tsfb + 8 * j + 4 * rb,
+                                     sdesc_sf_chunk(ssfb + rb * (kKBlocksPerTile * kSfChunk) + j * kSfChunk));
+            for (int j = 0; j < nkb; ++j) {
+              tc_mma_nvf4(tmem + kAccCol, sdesc_kmajor_sw128(sa + 32 * j), sdesc_kmajor_sw128(sb + 32 * j), idesc,
+                          tsfa + 4 * j, tsfb + 8 * j, (kt | j) != 0 ? 1u : 0u);
+            }
           }
           tc_commit(&empty[stage]);
         }
