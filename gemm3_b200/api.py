@@ -145,7 +145,7 @@ def _launch_config(m, k, cfg, attrs):
         return c
     c = _lib.GemmConfig()
     c.struct_size = ctypes.sizeof(_lib.GemmConfig)
-    c.tile_m = 128
+    c.tile_m = 256 if cfg.tile[0] == 256 else 128  # 256: CTA-pair kernel, 128: one CTA per tile
     c.tile_n = 256
     m_tiles = -(-m // 128)
     s = int(attrs.get("fast_swz", 1) or 1)

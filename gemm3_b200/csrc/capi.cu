@@ -10,6 +10,7 @@
 
 #include "../../include/nvfp4_gemm.h"
 #include "gemm_kernel.cuh"
+#include "gemm_pair_kernel.cuh"
 #include "quant_kernel.cuh"
 
 namespace {
@@ -37,6 +38,7 @@ struct DeviceCache {
   int cc_major = 0, cc_minor = 0;
   int64_t l2_bytes = 0;
   bool gemm_attr_set = false;
+  int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
 };
 DeviceCache g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -96,8 +98,43 @@ int ensure_gemm_attributes(DeviceCache* d) {
                                g3::kGemmSmemBytes));
   G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                g3::kGemmSmemBytes));
+  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g3::kPairSmemBytes));
+  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g3::kPairSmemBytes));
+  // How many CTA pairs fit at once (SMs that cannot be paired inside a GPC stay idle).
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(2 * (d->sm_count / 2), 1, 1);
+  lc.blockDim = dim3(g3::kGemmThreads, 1, 1);
+  lc.dynamicSmemBytes = g3::kPairSmemBytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  lc.attrs = &attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, g3::nvfp4_gemm_pair_kernel<true>, &lc) != cudaSuccess || n < 1) {
+    (void)cudaGetLastError();
+    n = d->sm_count / 2;
+  }
+  d->pair_clusters = n;
   d->gemm_attr_set = true;
   return NVFP4_OK;
+}
+
+// 3-D uint32 view of a swizzled scale tensor: {128 words = one 512-byte chunk, 64-element block,
+// 128-row block}; boxes of `box_rb` row blocks x 4 blocks. Out-of-range blocks read as zero.
+int encode_scales(CUtensorMap* m, const void* base, int64_t rowblocks, int64_t kblocks, uint32_t box_rb) {
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(kblocks), static_cast<cuuint64_t>(rowblocks)};
+  cuuint64_t strides[2] = {512, static_cast<cuuint64_t>(kblocks) * 512};
+  cuuint32_t box[3] = {128, static_cast<cuuint32_t>(g3::kKBlocksPerTile), box_rb};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NVFP4_OK : NVFP4_ERR_TENSOR_MAP;
 }
 
 int grid_for(int64_t work, int sm_count, int threads = 256) {
@@ -198,7 +235,9 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
     return NVFP4_ERR_MISALIGNED;
   nvfp4_gemm_config def = {};
   if (cfg != nullptr && cfg->struct_size >= static_cast<int32_t>(sizeof(nvfp4_gemm_config))) def = *cfg;
-  if ((def.tile_m != 0 && def.tile_m != 128) || (def.tile_n != 0 && def.tile_n != 256)) return NVFP4_ERR_INVALID_VALUE;
+  if ((def.tile_m != 0 && def.tile_m != 128 && def.tile_m != 256) || (def.tile_n != 0 && def.tile_n != 256))
+    return NVFP4_ERR_INVALID_VALUE;
+  const bool pair = def.tile_m != 128;
   if (def.raster_band < 0) return NVFP4_ERR_INVALID_VALUE;
 
   int dev = 0;
@@ -211,11 +250,17 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   rc = get_encoder();
   if (rc != NVFP4_OK) return rc;
 
-  CUtensorMap tmap_a, tmap_b;
+  CUtensorMap tmap_a, tmap_b, tmap_sfa, tmap_sfb;
   rc = encode_operand(&tmap_a, a, m, k / 2, g3::kTileM);
   if (rc != NVFP4_OK) return rc;
-  rc = encode_operand(&tmap_b, b, n, k / 2, g3::kTileN);
+  rc = encode_operand(&tmap_b, b, n, k / 2, pair ? 128 : g3::kTileN);
   if (rc != NVFP4_OK) return rc;
+  if (pair) {
+    rc = encode_scales(&tmap_sfa, sfa, (m + 127) / 128, k / 64, 1);
+    if (rc != NVFP4_OK) return rc;
+    rc = encode_scales(&tmap_sfb, sfb, (n + 127) / 128, k / 64, 2);
+    if (rc != NVFP4_OK) return rc;
+  }
 
   g3::GemmParams p;
   p.sfa = static_cast<const uint8_t*>(sfa);
@@ -226,7 +271,8 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  p.m_tiles = static_cast<int>((m + g3::kTileM - 1) / g3::kTileM);
+  const int tile_rows = pair ? g3::kPairTileM : g3::kTileM;
+  p.m_tiles = static_cast<int>((m + tile_rows - 1) / tile_rows);
   p.n_tiles = static_cast<int>((n + g3::kTileN - 1) / g3::kTileN);
   p.k_tiles = static_cast<int>((k + 255) / 256);
   p.sf_kblocks = static_cast<int>(k / 64);
@@ -234,7 +280,8 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
   if (tiles > INT32_MAX) return NVFP4_ERR_INVALID_VALUE;
   p.num_tiles = static_cast<int>(tiles);
-  p.raster_band = def.raster_band;
+  // raster_band counts 128-row tiles; the pair kernel's tiles are 256 rows
+  p.raster_band = pair ? (def.raster_band + 1) / 2 : def.raster_band;
   p.raster_along_m = def.raster_along_m;
   p.pol_a = def.l2_policy_a;
   p.pol_b = def.l2_policy_b;
@@ -244,17 +291,38 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   p.pace_ns = def.epi_store_pace_ns;
   p.tma_b_first = def.tma_b_first;
 
-  int ctas = d->sm_count;
-  if (def.max_ctas > 0 && def.max_ctas < ctas) ctas = def.max_ctas;
-  if (ctas > p.num_tiles) ctas = p.num_tiles;
-
   rc = ensure_gemm_attributes(d);
   if (rc != NVFP4_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (out_dtype == NVFP4_DTYPE_BF16)
-    g3::nvfp4_gemm_kernel<true><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
-  else
-    g3::nvfp4_gemm_kernel<false><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+  if (pair) {
+    int pairs = d->pair_clusters;
+    if (def.max_ctas > 0 && def.max_ctas / 2 < pairs) pairs = def.max_ctas / 2 > 0 ? def.max_ctas / 2 : 1;
+    if (pairs > p.num_tiles) pairs = p.num_tiles;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(2 * pairs, 1, 1);
+    lc.blockDim = dim3(g3::kGemmThreads, 1, 1);
+    lc.dynamicSmemBytes = g3::kPairSmemBytes;
+    lc.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    lc.attrs = &attr;
+    lc.numAttrs = 1;
+    if (out_dtype == NVFP4_DTYPE_BF16)
+      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_pair_kernel<true>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
+    else
+      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_pair_kernel<false>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
+  } else {
+    int ctas = d->sm_count;
+    if (def.max_ctas > 0 && def.max_ctas < ctas) ctas = def.max_ctas;
+    if (ctas > p.num_tiles) ctas = p.num_tiles;
+    if (out_dtype == NVFP4_DTYPE_BF16)
+      g3::nvfp4_gemm_kernel<true><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+    else
+      g3::nvfp4_gemm_kernel<false><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+  }
   G3_CUDA(cudaGetLastError());
   return NVFP4_OK;
 }

@@ -145,27 +145,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    // The whole warp walks the schedule; lane 0 waits and issues, the result of each wait is
-    // broadcast so the warp leaves the loop together.
-    const uint64_t pol_a = make_policy(p.pol_a);
-    const uint64_t pol_b = make_policy(p.pol_b);
-    const uint64_t pol_sfa = make_policy(p.pol_sfa);
-    const uint64_t pol_sfb = make_policy(p.pol_sfb);
-    uint32_t stage = 0, phase = 0;
-    uint32_t issued_mask = 0, issued_parity = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-      int mt, nt;
-      tile_coord(p, t, mt, nt);
-      const int nrb = min(2, p.n_rowblocks - 2 * nt);
-      for (int kt = 0; kt < p.k_tiles; ++kt) {
-        bool waited = true;
-        if (lane == 0) waited = mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag);
-        if (!__shfl_sync(0xffffffffu, waited, 0)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
+    // One thread walks the schedule. Warp-wide collectives inside this loop (a divergent wait
+    // followed by a shuffle or __syncwarp per k-tile) roughly halve the MMA issue rate.
+    if (lane == 0) {
+      const uint64_t pol_a = make_policy(p.pol_a);
+      const uint64_t pol_b = make_policy(p.pol_b);
+      const uint64_t pol_sfa = make_policy(p.pol_sfa);
+      const uint64_t pol_sfb = make_policy(p.pol_sfb);
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+        int mt, nt;
+        tile_coord(p, t, mt, nt);
+        const int nrb = min(2, p.n_rowblocks - 2 * nt);
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
           const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
           const uint32_t sf_bytes = static_cast<uint32_t>(nkb * kSfChunk);
           mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes + sf_bytes * (1 + nrb));
@@ -187,60 +185,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       p.sfb + (static_cast<size_t>(2 * nt + rb) * p.sf_kblocks + kb0) * kSfChunk, sf_bytes,
                       &full[stage], pol_sfb);
           }
-        }
-        __syncwarp();
-        issued_mask |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-    }
-    if (ok) {
-      // Tail: wait until the MMA warp has released every stage, so no tcgen05.commit arrival
-      // is still in flight when the CTA exits.
-      for (int s = 0; s < kStages; ++s) {
-        bool waited = true;
-        if (lane == 0) waited = mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag);
-        if (!__shfl_sync(0xffffffffu, waited, 0)) break;
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
-    }
-    if (!ok && lane == 0) {
-      // Unwind: let the copies already issued land before shared memory goes away.
-      for (int s = 0; s < kStages; ++s)
-        if (issued_mask & (1u << s))
-          mbar_wait(&full[s], (issued_parity >> s) & 1u, p.status, kStatusTimeoutDrain, nullptr);
+      if (ok) {
+        // Tail: wait until the MMA warp has released every stage, so no tcgen05.commit arrival
+        // is still in flight when the CTA exits.
+        for (int s = 0; s < kStages; ++s) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) break;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      } else {
+        // Unwind: let the copies already issued land before shared memory goes away.
+        for (int s = 0; s < kStages; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait(&full[s], (issued_parity >> s) & 1u, p.status, kStatusTimeoutDrain, nullptr);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_nvf4(kTileM, kTileN);
-    uint32_t stage = 0, phase = 0, acc_phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-      int mt, nt;
-      tile_coord(p, t, mt, nt);
-      const int nrb = min(2, p.n_rowblocks - 2 * nt);
-      bool waited = true;
-      if (lane == 0) waited = mbar_wait(acc_empty, acc_phase ^ 1u, p.status, kStatusTimeoutAccEmpty, abort_flag);
-      if (!__shfl_sync(0xffffffffu, waited, 0)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (lane == 0) waited = mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag);
-        if (!__shfl_sync(0xffffffffu, waited, 0)) {
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_nvf4(kTileM, kTileN);
+      uint32_t stage = 0, phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+        int mt, nt;
+        tile_coord(p, t, mt, nt);
+        const int nrb = min(2, p.n_rowblocks - 2 * nt);
+        if (!mbar_wait(acc_empty, acc_phase ^ 1u, p.status, kStatusTimeoutAccEmpty, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (lane == 0) {
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
           const uint32_t sa = smem_u32(smem + kOffA + stage * kABytes);
           const uint32_t sb = smem_u32(smem + kOffB + stage * kBBytes);
@@ -274,22 +265,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
           tc_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        tc_commit(acc_full);
+        acc_phase ^= 1u;
       }
-      if (!ok) break;
-      if (lane == 0) tc_commit(acc_full);
-      __syncwarp();
-      acc_phase ^= 1u;
-    }
-    if (!ok && lane == 0) {
-      // Unwind: wait for the MMAs already issued before TMEM is released.
-      tc_commit(drain);
-      mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, nullptr);
+      if (!ok) {
+        // Unwind: wait for the MMAs already issued before TMEM is released.
+        tc_commit(drain);
+        mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, nullptr);
+      }
     }
     __syncwarp();
   } else {

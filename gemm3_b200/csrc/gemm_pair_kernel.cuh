@@ -1,0 +1,289 @@
+// Persistent NVFP4 block-scaled GEMM on CTA pairs (tcgen05 cta_group::2) for sm_100a.
+//
+// A cluster of two CTAs on neighbouring SMs computes 256x256 output tiles. CTA r of the pair
+// owns output rows [m0 + 128 r, +128) and supplies B rows [n0 + 128 r, +128); one tcgen05.mma
+// (M=256, N=256, K=64) issued by CTA 0 reads A and B from both CTAs' shared memory and writes each
+// CTA's half of the accumulator into its own TMEM. Compared with one-CTA 128x256 tiles this halves
+// the B bytes every SM loads from L2 and reads from shared memory per FLOP.
+//
+// Roles (per CTA, 6 warps):
+//   warp 0      producer, in both CTAs: TMA loads of its A and B halves (128 rows x 128 B, 128-byte
+//               swizzle), its 128 rows of A scales and all 256 rows of B scales (3-D tensor maps
+//               over the swizzled scale layout), each completing on CTA 0's "full" barrier;
+//   warp 1      TMEM owner in both CTAs; in CTA 0 the MMA issuer: per 64-element block one A-scale
+//               and two B-scale tcgen05.cp (cta_group::2, into both TMEMs) and one MMA; commits
+//               release the stage in both CTAs and, per tile, hand the accumulator to both epilogues;
+//   warps 2-5   epilogue, in both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
+//               released to CTA 0's MMA warp, then 256-bit row stores.
+// No TMA multicast is used: every CTA loads what it needs itself. The accumulation order per
+// output element is k = 0, 64, 128, ... as in the one-CTA kernel, so both produce the same bits.
+#pragma once
+#include "gemm_kernel.cuh"
+
+namespace g3 {
+
+constexpr int kPairTileM = 256;
+constexpr int kPairTileN = 256;
+constexpr int kPairStages = 5;
+constexpr int kPairABytes = 128 * kTileKBytes;                 // this CTA's 128 A rows
+constexpr int kPairBBytes = 128 * kTileKBytes;                 // this CTA's 128 B rows
+constexpr int kPairSfaBytes = kKBlocksPerTile * kSfChunk;      // 128 rows x 16 scales
+constexpr int kPairSfbBytes = 2 * kKBlocksPerTile * kSfChunk;  // 256 rows x 16 scales
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes + kPairSfaBytes + kPairSfbBytes;
+constexpr uint32_t kPairTxBytes = 2u * kPairStageBytes;        // both CTAs complete on CTA 0's barrier
+
+constexpr int kPairOffA = 0;
+constexpr int kPairOffB = kPairOffA + kPairStages * kPairABytes;
+constexpr int kPairOffSfa = kPairOffB + kPairStages * kPairBBytes;
+constexpr int kPairOffSfb = kPairOffSfa + kPairStages * kPairSfaBytes;
+constexpr int kPairOffBar = kPairOffSfb + kPairStages * kPairSfbBytes;
+constexpr int kPairNumBars = 2 * kPairStages + 3;  // full[S], empty[S], acc_full, acc_empty, drain
+constexpr int kPairOffTmemSlot = kPairOffBar + kPairNumBars * 8;
+constexpr int kPairOffAbort = kPairOffTmemSlot + 4;
+constexpr int kPairSmemBytes = kPairOffAbort + 4 + 1024;
+
+// TMEM columns: accumulator [0, 256); per stage 16 A-scale + 32 B-scale columns.
+constexpr int kPairSfaCol = 256;
+constexpr int kPairSfColsPerStage = 4 * kKBlocksPerTile + 8 * kKBlocksPerTile;
+static_assert(kPairSfaCol + kPairStages * kPairSfColsPerStage <= kTmemCols, "pair scales do not fit in TMEM");
+static_assert(kPairSmemBytes <= 232448, "pair kernel exceeds shared memory");
+
+template <bool kBF16>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                           const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPairStages;
+  uint64_t* acc_full = bars + 2 * kPairStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairOffTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairOffAbort);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);   // one arrive.expect_tx by CTA 0's producer + both CTAs' bytes
+      mbar_init(&empty[s], 1);  // one commit from CTA 0's MMA warp
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * 4 * 32);  // every epilogue thread of both CTAs
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_sfa);
+    prefetch_tmap(&tmap_sfb);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // CTA 0's barriers as seen from either CTA of the pair.
+  const uint32_t full0 = mapa_shared(smem_u32(full), 0);
+  const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    // One thread walks the schedule (no warp collectives inside the loop).
+    if (lane == 0) {
+      const uint64_t pol_a = make_policy(p.pol_a);
+      const uint64_t pol_b = make_policy(p.pol_b);
+      const uint64_t pol_sfa = make_policy(p.pol_sfa);
+      const uint64_t pol_sfb = make_policy(p.pol_sfb);
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
+        int mt, nt;
+        tile_coord(p, t, mt, nt);
+        const int row_a = mt * kPairTileM + 128 * static_cast<int>(rank);
+        const int row_b = nt * kPairTileN + 128 * static_cast<int>(rank);
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = full0 + 8u * stage;
+          if (leader) mbar_arrive_expect_tx(&full[stage], kPairTxBytes);
+          const int kb0 = kKBlocksPerTile * kt;
+          uint8_t* sa = smem + kPairOffA + stage * kPairABytes;
+          uint8_t* sb = smem + kPairOffB + stage * kPairBBytes;
+          if (p.tma_b_first) {
+            tma_load_2d_pair(sb, &tmap_b, kt * kTileKBytes, row_b, bar, pol_b);
+            tma_load_2d_pair(sa, &tmap_a, kt * kTileKBytes, row_a, bar, pol_a);
+          } else {
+            tma_load_2d_pair(sa, &tmap_a, kt * kTileKBytes, row_a, bar, pol_a);
+            tma_load_2d_pair(sb, &tmap_b, kt * kTileKBytes, row_b, bar, pol_b);
+          }
+          // scale chunks: {512-byte chunk, 64-element block, 128-row block}
+          tma_load_3d_pair(smem + kPairOffSfa + stage * kPairSfaBytes, &tmap_sfa, 0, kb0, row_a >> 7, bar, pol_sfa);
+          tma_load_3d_pair(smem + kPairOffSfb + stage * kPairSfbBytes, &tmap_sfb, 0, kb0, 2 * nt, bar, pol_sfb);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        // Tail: every stage released by CTA 0's MMA warp, so no commit is still in flight.
+        for (int s = 0; s < kPairStages; ++s) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) break;
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      } else if (leader) {
+        for (int s = 0; s < kPairStages; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait(&full[s], (issued_parity >> s) & 1u, p.status, kStatusTimeoutDrain, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (CTA 0, one thread)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_nvf4(kPairTileM, kPairTileN);
+      const uint32_t empty_self = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), 1);
+      const uint32_t accf_self = smem_u32(acc_full), accf_peer = mapa_shared(smem_u32(acc_full), 1);
+      uint32_t stage = 0, phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
+        if (!mbar_wait(acc_empty, acc_phase ^ 1u, p.status, kStatusTimeoutAccEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
+          const uint64_t da = sdesc_kmajor_sw128(smem_u32(smem + kPairOffA + stage * kPairABytes));
+          const uint64_t db = sdesc_kmajor_sw128(smem_u32(smem + kPairOffB + stage * kPairBBytes));
+          const uint64_t dsa = sdesc_sf_chunk(smem_u32(smem + kPairOffSfa + stage * kPairSfaBytes));
+          const uint64_t dsb = sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + stage * kPairSfbBytes));
+          const uint32_t tsfa = tmem + kPairSfaCol + stage * kPairSfColsPerStage;
+          const uint32_t tsfb = tsfa + 4 * kKBlocksPerTile;
+          if (nkb == kKBlocksPerTile) {
+#pragma unroll
+            for (int j = 0; j < kKBlocksPerTile; ++j) {
+              tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
+              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
+              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+              tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
+                               (kt | j) != 0 ? 1u : 0u);
+            }
+          } else {
+            for (int j = 0; j < nkb; ++j) {
+              tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
+              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
+              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+              tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
+                               (kt | j) != 0 ? 1u : 0u);
+            }
+          }
+          tc_commit_pair(empty_self + 8u * stage);
+          tc_commit_pair(empty_peer + 8u * stage);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(accf_self);
+        tc_commit_pair(accf_peer);
+        acc_phase ^= 1u;
+      }
+      if (!ok) {
+        tc_commit_pair(smem_u32(drain));
+        mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, nullptr);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t tmem_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float alpha = *p.alpha;
+    const bool evict_first = p.store_evict_first != 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < p.num_tiles; t += num_pairs) {
+      int mt, nt;
+      tile_coord(p, t, mt, nt);
+      if (!mbar_wait(acc_full, acc_phase, p.status, kStatusTimeoutAccFull, abort_flag)) break;
+      acc_phase ^= 1u;
+      tc_fence_after();
+      uint32_t out[kPairTileN / 2];
+#pragma unroll
+      for (int ch = 0; ch < kPairTileN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_row + kAccCol + ch * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          out[ch * 16 + i] = pack_out(__fmul_rn(__uint_as_float(r[2 * i]), alpha),
+                                      __fmul_rn(__uint_as_float(r[2 * i + 1]), alpha), kBF16);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty0);
+
+      const int gm = mt * kPairTileM + 128 * static_cast<int>(rank) + row;
+      if (gm < p.m) {
+        uint8_t* rowp = reinterpret_cast<uint8_t*>(p.c) +
+                        (static_cast<size_t>(gm) * p.n + static_cast<size_t>(nt) * kPairTileN) * 2;
+        const int cols_left = p.n - nt * kPairTileN;
+#pragma unroll
+        for (int ch = 0; ch < kPairTileN / 32; ++ch) {
+          if (ch * 32 < cols_left) {
+            uint32_t v0[8], v1[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              v0[i] = out[ch * 16 + i];
+              v1[i] = out[ch * 16 + 8 + i];
+            }
+            if (evict_first) {
+              st_global_v8_ef(rowp + ch * 64, v0);
+              st_global_v8_ef(rowp + ch * 64 + 32, v1);
+            } else {
+              st_global_v8(rowp + ch * 64, v0);
+              st_global_v8(rowp + ch * 64 + 32, v1);
+            }
+            if (p.pace_ns > 0 && ch + 1 < kPairTileN / 32) __nanosleep(p.pace_ns);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+}  // namespace g3

@@ -53,7 +53,7 @@ enum { NVFP4_L2_NORMAL = 0, NVFP4_L2_EVICT_FIRST = 1, NVFP4_L2_EVICT_LAST = 2 };
  */
 typedef struct nvfp4_gemm_config {
   int32_t struct_size;           /* sizeof(nvfp4_gemm_config) */
-  int32_t tile_m;                /* 128: one CTA per tile (only value in this version); 0 = 128 */
+  int32_t tile_m;                /* 256 (or 0): CTA pairs, 256x256 tiles; 128: one CTA per 128x256 tile */
   int32_t tile_n;                /* 256 (only value in this version); 0 = 256 */
   int32_t raster_band;           /* 128-row tiles per raster band (0 or 1: bands of one tile) */
   int32_t raster_along_m;        /* 0: bands of M-tiles, sweep N ("N sweep"); 1: bands of N-tiles */
