@@ -105,7 +105,7 @@ int ensure_gemm_attributes(DeviceCache* d) {
   // How many CTA pairs fit at once (SMs that cannot be paired inside a GPC stay idle).
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(2 * (d->sm_count / 2), 1, 1);
-  lc.blockDim = dim3(g3::kGemmThreads, 1, 1);
+  lc.blockDim = dim3(g3::kPairThreads, 1, 1);
   lc.dynamicSmemBytes = g3::kPairSmemBytes;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -300,7 +300,7 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
     if (pairs > p.num_tiles) pairs = p.num_tiles;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(2 * pairs, 1, 1);
-    lc.blockDim = dim3(g3::kGemmThreads, 1, 1);
+    lc.blockDim = dim3(g3::kPairThreads, 1, 1);
     lc.dynamicSmemBytes = g3::kPairSmemBytes;
     lc.stream = s;
     cudaLaunchAttribute attr;

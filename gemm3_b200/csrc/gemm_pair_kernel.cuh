@@ -6,14 +6,19 @@
 // CTA's half of the accumulator into its own TMEM. Compared with one-CTA 128x256 tiles this halves
 // the B bytes every SM loads from L2 and reads from shared memory per FLOP.
 //
-// Roles (per CTA, 6 warps):
+// Roles (per CTA, 8 warps):
 //   warp 0      producer, in both CTAs: TMA loads of its A and B halves (128 rows x 128 B, 128-byte
 //               swizzle), its 128 rows of A scales and all 256 rows of B scales (3-D tensor maps
 //               over the swizzled scale layout), each completing on CTA 0's "full" barrier;
-//   warp 1      TMEM owner in both CTAs; in CTA 0 the MMA issuer: per 64-element block one A-scale
-//               and two B-scale tcgen05.cp (cta_group::2, into both TMEMs) and one MMA; commits
-//               release the stage in both CTAs and, per tile, hand the accumulator to both epilogues;
-//   warps 2-5   epilogue, in both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
+//   warp 1      TMEM owner in both CTAs; in CTA 0 the MMA issuer: one tcgen05.mma (cta_group::2)
+//               per 64-element block; commits release the stage in both CTAs and, per tile, hand
+//               the accumulator to both epilogues;
+//   warps 2, 3  in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 2 one
+//               A-scale chunk per 64-element block, warp 3 the two B-scale chunks. Every tcgen05
+//               instruction costs its issuing thread ~50 cycles, so one thread issuing three
+//               copies and one MMA per block (~200 cycles) could not keep up with the 128-cycle
+//               MMA; split over three threads each stays under it;
+//   warps 4-7   epilogue, in both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
 //               released to CTA 0's MMA warp, then 256-bit row stores.
 // No TMA multicast is used: every CTA loads what it needs itself. The accumulation order per
 // output element is k = 0, 64, 128, ... as in the one-CTA kernel, so both produce the same bits.
@@ -37,7 +42,9 @@ constexpr int kPairOffB = kPairOffA + kPairStages * kPairABytes;
 constexpr int kPairOffSfa = kPairOffB + kPairStages * kPairBBytes;
 constexpr int kPairOffSfb = kPairOffSfa + kPairStages * kPairSfaBytes;
 constexpr int kPairOffBar = kPairOffSfb + kPairStages * kPairSfbBytes;
-constexpr int kPairNumBars = 2 * kPairStages + 3;  // full[S], empty[S], acc_full, acc_empty, drain
+// full[S], empty[S], sfa_ready[S], sfb_ready[S], acc_full, acc_empty, drain[3] (one per tcgen05 issuer)
+constexpr int kPairNumBars = 4 * kPairStages + 5;
+constexpr int kPairThreads = 256;
 constexpr int kPairOffTmemSlot = kPairOffBar + kPairNumBars * 8;
 constexpr int kPairOffAbort = kPairOffTmemSlot + 4;
 constexpr int kPairSmemBytes = kPairOffAbort + 4 + 1024;
@@ -49,7 +56,7 @@ static_assert(kPairSfaCol + kPairStages * kPairSfColsPerStage <= kTmemCols, "pai
 static_assert(kPairSmemBytes <= 232448, "pair kernel exceeds shared memory");
 
 template <bool kBF16>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                            const GemmParams p) {
@@ -58,9 +65,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + kPairStages;
-  uint64_t* acc_full = bars + 2 * kPairStages;
+  uint64_t* sfa_ready = bars + 2 * kPairStages;
+  uint64_t* sfb_ready = bars + 3 * kPairStages;
+  uint64_t* acc_full = bars + 4 * kPairStages;
   uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_full + 2;
+  uint64_t* drain = acc_full + 2;  // [0] MMA, [1] A scales, [2] B scales
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairOffAbort);
 
@@ -75,10 +84,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&full[s], 1);   // one arrive.expect_tx by CTA 0's producer + both CTAs' bytes
       mbar_init(&empty[s], 1);  // one commit from CTA 0's MMA warp
+      mbar_init(&sfa_ready[s], 1);
+      mbar_init(&sfb_ready[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 4 * 32);  // every epilogue thread of both CTAs
-    mbar_init(drain, 1);
+    for (int d = 0; d < 3; ++d) mbar_init(&drain[d], 1);
     *abort_flag = 0;
     fence_mbarrier_init();
     prefetch_tmap(&tmap_a);
@@ -178,31 +189,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
+          if (!mbar_wait(&sfa_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag) ||
+              !mbar_wait(&sfb_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
           const uint64_t da = sdesc_kmajor_sw128(smem_u32(smem + kPairOffA + stage * kPairABytes));
           const uint64_t db = sdesc_kmajor_sw128(smem_u32(smem + kPairOffB + stage * kPairBBytes));
-          const uint64_t dsa = sdesc_sf_chunk(smem_u32(smem + kPairOffSfa + stage * kPairSfaBytes));
-          const uint64_t dsb = sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + stage * kPairSfbBytes));
           const uint32_t tsfa = tmem + kPairSfaCol + stage * kPairSfColsPerStage;
           const uint32_t tsfb = tsfa + 4 * kKBlocksPerTile;
           if (nkb == kKBlocksPerTile) {
 #pragma unroll
-            for (int j = 0; j < kKBlocksPerTile; ++j) {
-              tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
-              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
-              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+            for (int j = 0; j < kKBlocksPerTile; ++j)
               tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
                                (kt | j) != 0 ? 1u : 0u);
-            }
           } else {
-            for (int j = 0; j < nkb; ++j) {
-              tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
-              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
-              tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+            for (int j = 0; j < nkb; ++j)
               tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
                                (kt | j) != 0 ? 1u : 0u);
-            }
           }
           tc_commit_pair(empty_self + 8u * stage);
           tc_commit_pair(empty_peer + 8u * stage);
@@ -219,6 +225,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) {
         tc_commit_pair(smem_u32(drain));
         mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------ scale copies (CTA 0)
+    // Warp 2 copies the A scales (one 512-byte chunk per 64-element block), warp 3 the B scales
+    // (two chunks per block, rows 0-127 and 128-255 of the tile), each into the stage's TMEM
+    // region, then commits to that stage's ready barrier. The region of a stage is rewritten only
+    // after the stage has been refilled, i.e. after the MMAs that read it have completed.
+    if (leader && lane == 0) {
+      const bool is_a = warp == 2;
+      uint64_t* ready = is_a ? sfa_ready : sfb_ready;
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
+          const uint32_t tsfa = tmem + kPairSfaCol + stage * kPairSfColsPerStage;
+          const uint32_t tsfb = tsfa + 4 * kKBlocksPerTile;
+          if (is_a) {
+            const uint64_t dsa = sdesc_sf_chunk(smem_u32(smem + kPairOffSfa + stage * kPairSfaBytes));
+            if (nkb == kKBlocksPerTile) {
+#pragma unroll
+              for (int j = 0; j < kKBlocksPerTile; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
+            } else {
+              for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
+            }
+          } else {
+            const uint64_t dsb = sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + stage * kPairSfbBytes));
+            if (nkb == kKBlocksPerTile) {
+#pragma unroll
+              for (int j = 0; j < kKBlocksPerTile; ++j) {
+                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
+                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+              }
+            } else {
+              for (int j = 0; j < nkb; ++j) {
+                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
+                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
+              }
+            }
+          }
+          tc_commit_pair(smem_u32(&ready[stage]));
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        tc_commit_pair(smem_u32(&drain[warp - 1]));
+        mbar_wait(&drain[warp - 1], 0, p.status, kStatusTimeoutDrain, nullptr);
       }
     }
     __syncwarp();
