@@ -17,7 +17,8 @@
 //               A-scale chunk per 64-element block, warp 3 the two B-scale chunks. Every tcgen05
 //               instruction costs its issuing thread ~50 cycles, so one thread issuing three
 //               copies and one MMA per block (~200 cycles) could not keep up with the 128-cycle
-//               MMA; split over three threads each stays under it;
+//               MMA; split over three threads each stays under it. The copy warps hand a stage
+//               over once its copies are issued (fence + mbarrier arrive), not completed;
 //   warps 4-7   epilogue, in both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
 //               released to CTA 0's MMA warp, then 256-bit row stores.
 // No TMA multicast is used: every CTA loads what it needs itself. The accumulation order per
@@ -272,7 +273,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               }
             }
           }
-          tc_commit_pair(smem_u32(&ready[stage]));
+          // Hand the stage to the MMA thread as soon as the copies are issued: the fence orders
+          // them before this arrive, the MMA thread's after_thread_sync fence orders its MMAs
+          // after it, and the tensor pipe runs them in that order. Waiting for the copies to
+          // complete instead (tcgen05.commit) would drain the pipe once per k-tile.
+          tc_fence_before();
+          mbar_arrive(&ready[stage]);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1u;
