@@ -6,20 +6,26 @@
 // CTA's half of the accumulator into its own TMEM. Compared with one-CTA 128x256 tiles this halves
 // the B bytes every SM loads from L2 and reads from shared memory per FLOP.
 //
-// Roles (per CTA, 8 warps):
-//   warp 0      producer, in both CTAs: TMA loads of its A and B halves (128 rows x 128 B, 128-byte
-//               swizzle), its 128 rows of A scales and all 256 rows of B scales (3-D tensor maps
-//               over the swizzled scale layout), each completing on CTA 0's "full" barrier;
+// Two shared-memory rings feed the MMA: a 5-stage ring of A/B k-tiles (32 KiB per CTA per stage)
+// and an 8-slot ring of scale k-tiles (6 KiB). The scale ring runs ahead, so the scale copies into
+// TMEM are issued before the A/B data of the same k-tile lands and stay off the critical path.
+// Scales sit in TMEM in one 48-column region per A/B stage.
+//
+// Roles (per CTA, 9 warps):
+//   warp 0      A/B producer, both CTAs: TMA loads of its A and B halves (128 rows x 128 B,
+//               128-byte swizzle), completing on CTA 0's "full" barrier of the stage;
+//   warp 2      scale producer, both CTAs: TMA loads of its 128 rows of A scales and all 256 rows
+//               of B scales (3-D tensor maps over the swizzled layout), on CTA 0's "sf_full";
 //   warp 1      TMEM owner in both CTAs; in CTA 0 the MMA issuer: one tcgen05.mma (cta_group::2)
-//               per 64-element block; commits release the stage in both CTAs and, per tile, hand
-//               the accumulator to both epilogues;
-//   warps 2, 3  in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 2 one
-//               A-scale chunk per 64-element block, warp 3 the two B-scale chunks. Every tcgen05
-//               instruction costs its issuing thread ~50 cycles, so one thread issuing three
-//               copies and one MMA per block (~200 cycles) could not keep up with the 128-cycle
-//               MMA; split over three threads each stays under it. The copy warps hand a stage
-//               over once its copies are issued (fence + mbarrier arrive), not completed;
-//   warps 4-7   epilogue, in both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
+//               per 64-element block; commits release the A/B stage in both CTAs and, per tile,
+//               hand the accumulator to both epilogues;
+//   warps 3, 4  in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 3 one
+//               A-scale chunk per 64-element block, warp 4 the two B-scale chunks. Every tcgen05
+//               instruction costs its issuing thread ~50 cycles, so the three copies and the MMA
+//               of a block are spread over three threads. A copy warp hands its TMEM region to the
+//               MMA thread once the copies are issued (fence + mbarrier arrive) and frees the
+//               shared-memory slot through a commit when they have completed;
+//   warps 5-8   epilogue, both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
 //               released to CTA 0's MMA warp, then 256-bit row stores.
 // No TMA multicast is used: every CTA loads what it needs itself. The accumulation order per
 // output element is k = 0, 64, 128, ... as in the one-CTA kernel, so both produce the same bits.
@@ -30,27 +36,29 @@ namespace g3 {
 
 constexpr int kPairTileM = 256;
 constexpr int kPairTileN = 256;
-constexpr int kPairStages = 5;
+constexpr int kPairStages = 5;    // A/B ring
+constexpr int kPairSfSlots = 8;   // scale ring
 constexpr int kPairABytes = 128 * kTileKBytes;                 // this CTA's 128 A rows
 constexpr int kPairBBytes = 128 * kTileKBytes;                 // this CTA's 128 B rows
 constexpr int kPairSfaBytes = kKBlocksPerTile * kSfChunk;      // 128 rows x 16 scales
 constexpr int kPairSfbBytes = 2 * kKBlocksPerTile * kSfChunk;  // 256 rows x 16 scales
-constexpr int kPairStageBytes = kPairABytes + kPairBBytes + kPairSfaBytes + kPairSfbBytes;
-constexpr uint32_t kPairTxBytes = 2u * kPairStageBytes;        // both CTAs complete on CTA 0's barrier
+constexpr uint32_t kPairAbTx = 2u * (kPairABytes + kPairBBytes);     // both CTAs, on CTA 0's barrier
+constexpr uint32_t kPairSfTx = 2u * (kPairSfaBytes + kPairSfbBytes);
 
 constexpr int kPairOffA = 0;
 constexpr int kPairOffB = kPairOffA + kPairStages * kPairABytes;
 constexpr int kPairOffSfa = kPairOffB + kPairStages * kPairBBytes;
-constexpr int kPairOffSfb = kPairOffSfa + kPairStages * kPairSfaBytes;
-constexpr int kPairOffBar = kPairOffSfb + kPairStages * kPairSfbBytes;
-// full[S], empty[S], sfa_ready[S], sfb_ready[S], acc_full, acc_empty, drain[3] (one per tcgen05 issuer)
-constexpr int kPairNumBars = 4 * kPairStages + 5;
-constexpr int kPairThreads = 256;
+constexpr int kPairOffSfb = kPairOffSfa + kPairSfSlots * kPairSfaBytes;
+constexpr int kPairOffBar = kPairOffSfb + kPairSfSlots * kPairSfbBytes;
+// full[S], empty[S], sfa_ready[S], sfb_ready[S], sf_full[Q], sf_empty[Q], acc_full, acc_empty,
+// drain[3] (one per tcgen05 issuer)
+constexpr int kPairNumBars = 4 * kPairStages + 2 * kPairSfSlots + 5;
+constexpr int kPairThreads = 288;
 constexpr int kPairOffTmemSlot = kPairOffBar + kPairNumBars * 8;
 constexpr int kPairOffAbort = kPairOffTmemSlot + 4;
 constexpr int kPairSmemBytes = kPairOffAbort + 4 + 1024;
 
-// TMEM columns: accumulator [0, 256); per stage 16 A-scale + 32 B-scale columns.
+// TMEM columns: accumulator [0, 256); per A/B stage 16 A-scale + 32 B-scale columns.
 constexpr int kPairSfaCol = 256;
 constexpr int kPairSfColsPerStage = 4 * kKBlocksPerTile + 8 * kKBlocksPerTile;
 static_assert(kPairSfaCol + kPairStages * kPairSfColsPerStage <= kTmemCols, "pair scales do not fit in TMEM");
@@ -65,10 +73,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBar);
   uint64_t* full = bars;
-  uint64_t* empty = bars + kPairStages;
-  uint64_t* sfa_ready = bars + 2 * kPairStages;
-  uint64_t* sfb_ready = bars + 3 * kPairStages;
-  uint64_t* acc_full = bars + 4 * kPairStages;
+  uint64_t* empty = full + kPairStages;
+  uint64_t* sfa_ready = empty + kPairStages;
+  uint64_t* sfb_ready = sfa_ready + kPairStages;
+  uint64_t* sf_full = sfb_ready + kPairStages;
+  uint64_t* sf_empty = sf_full + kPairSfSlots;
+  uint64_t* acc_full = sf_empty + kPairSfSlots;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_full + 2;  // [0] MMA, [1] A scales, [2] B scales
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairOffTmemSlot);
@@ -83,10 +93,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&full[s], 1);   // one arrive.expect_tx by CTA 0's producer + both CTAs' bytes
-      mbar_init(&empty[s], 1);  // one commit from CTA 0's MMA warp
+      mbar_init(&full[s], 1);   // one arrive.expect_tx by CTA 0's A/B producer + both CTAs' bytes
+      mbar_init(&empty[s], 1);  // one commit from CTA 0's MMA thread
       mbar_init(&sfa_ready[s], 1);
       mbar_init(&sfb_ready[s], 1);
+    }
+    for (int q = 0; q < kPairSfSlots; ++q) {
+      mbar_init(&sf_full[q], 1);   // one arrive.expect_tx by CTA 0's scale producer
+      mbar_init(&sf_empty[q], 2);  // one commit from each copy warp
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 4 * 32);  // every epilogue thread of both CTAs
@@ -109,16 +123,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   // CTA 0's barriers as seen from either CTA of the pair.
   const uint32_t full0 = mapa_shared(smem_u32(full), 0);
+  const uint32_t sf_full0 = mapa_shared(smem_u32(sf_full), 0);
   const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (both CTAs)
-    // One thread walks the schedule (no warp collectives inside the loop).
+    // ------------------------------------------------------------------ A/B producer (both CTAs)
+    // One thread walks the schedule (warp collectives inside the loop halve the issue rate).
     if (lane == 0) {
       const uint64_t pol_a = make_policy(p.pol_a);
       const uint64_t pol_b = make_policy(p.pol_b);
-      const uint64_t pol_sfa = make_policy(p.pol_sfa);
-      const uint64_t pol_sfb = make_policy(p.pol_sfb);
       uint32_t stage = 0, phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
@@ -133,8 +146,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             break;
           }
           const uint32_t bar = full0 + 8u * stage;
-          if (leader) mbar_arrive_expect_tx(&full[stage], kPairTxBytes);
-          const int kb0 = kKBlocksPerTile * kt;
+          if (leader) mbar_arrive_expect_tx(&full[stage], kPairAbTx);
           uint8_t* sa = smem + kPairOffA + stage * kPairABytes;
           uint8_t* sb = smem + kPairOffB + stage * kPairBBytes;
           if (p.tma_b_first) {
@@ -144,9 +156,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             tma_load_2d_pair(sa, &tmap_a, kt * kTileKBytes, row_a, bar, pol_a);
             tma_load_2d_pair(sb, &tmap_b, kt * kTileKBytes, row_b, bar, pol_b);
           }
-          // scale chunks: {512-byte chunk, 64-element block, 128-row block}
-          tma_load_3d_pair(smem + kPairOffSfa + stage * kPairSfaBytes, &tmap_sfa, 0, kb0, row_a >> 7, bar, pol_sfa);
-          tma_load_3d_pair(smem + kPairOffSfb + stage * kPairSfbBytes, &tmap_sfb, 0, kb0, 2 * nt, bar, pol_sfb);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kPairStages) {
@@ -156,7 +165,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
       if (ok) {
-        // Tail: every stage released by CTA 0's MMA warp, so no commit is still in flight.
+        // Tail: every stage released by CTA 0's MMA thread, so no commit is still in flight.
         for (int s = 0; s < kPairStages; ++s) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) break;
           if (++stage == kPairStages) {
@@ -168,6 +177,52 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int s = 0; s < kPairStages; ++s)
           if (issued_mask & (1u << s))
             mbar_wait(&full[s], (issued_parity >> s) & 1u, p.status, kStatusTimeoutDrain, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ scale producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol_sfa = make_policy(p.pol_sfa);
+      const uint64_t pol_sfb = make_policy(p.pol_sfb);
+      uint32_t slot = 0, phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
+        int mt, nt;
+        tile_coord(p, t, mt, nt);
+        const int rb_a = (mt * kPairTileM + 128 * static_cast<int>(rank)) >> 7;
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!mbar_wait(&sf_empty[slot], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = sf_full0 + 8u * slot;
+          if (leader) mbar_arrive_expect_tx(&sf_full[slot], kPairSfTx);
+          // scale chunks: {512-byte chunk, 64-element block, 128-row block}
+          const int kb0 = kKBlocksPerTile * kt;
+          tma_load_3d_pair(smem + kPairOffSfa + slot * kPairSfaBytes, &tmap_sfa, 0, kb0, rb_a, bar, pol_sfa);
+          tma_load_3d_pair(smem + kPairOffSfb + slot * kPairSfbBytes, &tmap_sfb, 0, kb0, 2 * nt, bar, pol_sfb);
+          issued_mask |= 1u << slot;
+          issued_parity = (issued_parity & ~(1u << slot)) | (phase << slot);
+          if (++slot == kPairSfSlots) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        for (int q = 0; q < kPairSfSlots; ++q) {
+          if (!mbar_wait(&sf_empty[slot], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) break;
+          if (++slot == kPairSfSlots) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      } else if (leader) {
+        for (int q = 0; q < kPairSfSlots; ++q)
+          if (issued_mask & (1u << q))
+            mbar_wait(&sf_full[q], (issued_parity >> q) & 1u, p.status, kStatusTimeoutDrain, nullptr);
       }
     }
     __syncwarp();
@@ -186,12 +241,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         tc_fence_after();
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
-            ok = false;
-            break;
-          }
           if (!mbar_wait(&sfa_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag) ||
-              !mbar_wait(&sfb_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+              !mbar_wait(&sfb_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag) ||
+              !mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
             ok = false;
             break;
           }
@@ -224,25 +276,27 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         acc_phase ^= 1u;
       }
       if (!ok) {
-        tc_commit_pair(smem_u32(drain));
-        mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, nullptr);
+        tc_commit_pair(smem_u32(&drain[0]));
+        mbar_wait(&drain[0], 0, p.status, kStatusTimeoutDrain, nullptr);
       }
     }
     __syncwarp();
-  } else if (warp == 2 || warp == 3) {
+  } else if (warp == 3 || warp == 4) {
     // ------------------------------------------------------------------ scale copies (CTA 0)
-    // Warp 2 copies the A scales (one 512-byte chunk per 64-element block), warp 3 the B scales
-    // (two chunks per block, rows 0-127 and 128-255 of the tile), each into the stage's TMEM
-    // region, then commits to that stage's ready barrier. The region of a stage is rewritten only
-    // after the stage has been refilled, i.e. after the MMAs that read it have completed.
+    // Warp 3 copies the A scales (one 512-byte chunk per 64-element block), warp 4 the B scales
+    // (two chunks per block, tile rows 0-127 and 128-255). K-tile g lands in scale slot g % 8 and
+    // is copied into the TMEM region of A/B stage g % 5 once the MMAs of k-tile g - 5, the last
+    // readers of that region, have completed.
     if (leader && lane == 0) {
-      const bool is_a = warp == 2;
+      const bool is_a = warp == 3;
       uint64_t* ready = is_a ? sfa_ready : sfb_ready;
-      uint32_t stage = 0, phase = 0;
+      const uint32_t sfe_self = smem_u32(sf_empty), sfe_peer = mapa_shared(smem_u32(sf_empty), 1);
+      uint32_t stage = 0, phase = 0, slot = 0, sphase = 0;
       bool ok = true;
       for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+          if (!mbar_wait(&sf_full[slot], sphase, p.status, kStatusTimeoutFull, abort_flag) ||
+              !mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
             ok = false;
             break;
           }
@@ -251,7 +305,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint32_t tsfa = tmem + kPairSfaCol + stage * kPairSfColsPerStage;
           const uint32_t tsfb = tsfa + 4 * kKBlocksPerTile;
           if (is_a) {
-            const uint64_t dsa = sdesc_sf_chunk(smem_u32(smem + kPairOffSfa + stage * kPairSfaBytes));
+            const uint64_t dsa = sdesc_sf_chunk(smem_u32(smem + kPairOffSfa + slot * kPairSfaBytes));
             if (nkb == kKBlocksPerTile) {
 #pragma unroll
               for (int j = 0; j < kKBlocksPerTile; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
@@ -259,7 +313,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
             }
           } else {
-            const uint64_t dsb = sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + stage * kPairSfbBytes));
+            const uint64_t dsb = sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + slot * kPairSfbBytes));
             if (nkb == kKBlocksPerTile) {
 #pragma unroll
               for (int j = 0; j < kKBlocksPerTile; ++j) {
@@ -273,21 +327,27 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               }
             }
           }
-          // Hand the stage to the MMA thread as soon as the copies are issued: the fence orders
-          // them before this arrive, the MMA thread's after_thread_sync fence orders its MMAs
-          // after it, and the tensor pipe runs them in that order. Waiting for the copies to
-          // complete instead (tcgen05.commit) would drain the pipe once per k-tile.
+          // The TMEM region goes to the MMA thread as soon as the copies are issued: the fence
+          // orders them before this arrive, the MMA thread's after_thread_sync fence orders its
+          // MMAs after it, and the tensor pipe runs them in that order. The shared-memory slot
+          // is freed only when the copies have completed.
           tc_fence_before();
           mbar_arrive(&ready[stage]);
+          tc_commit_pair(sfe_self + 8u * slot);
+          tc_commit_pair(sfe_peer + 8u * slot);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1u;
           }
+          if (++slot == kPairSfSlots) {
+            slot = 0;
+            sphase ^= 1u;
+          }
         }
       }
       if (!ok) {
-        tc_commit_pair(smem_u32(&drain[warp - 1]));
-        mbar_wait(&drain[warp - 1], 0, p.status, kStatusTimeoutDrain, nullptr);
+        tc_commit_pair(smem_u32(&drain[warp - 2]));
+        mbar_wait(&drain[warp - 2], 0, p.status, kStatusTimeoutDrain, nullptr);
       }
     }
     __syncwarp();
@@ -306,15 +366,21 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       acc_phase ^= 1u;
       tc_fence_after();
       uint32_t out[kPairTileN / 2];
+      // Two 32-column loads in flight per wait: the MMA thread idles until the accumulator is
+      // drained, so the drain is kept to four TMEM round trips.
 #pragma unroll
-      for (int ch = 0; ch < kPairTileN / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_row + kAccCol + ch * 32, r);
+      for (int ch = 0; ch < kPairTileN / 32; ch += 2) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(tmem_row + kAccCol + ch * 32, r0);
+        tmem_ld_32x32b_x32(tmem_row + kAccCol + ch * 32 + 32, r1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          out[ch * 16 + i] = pack_out(__fmul_rn(__uint_as_float(r[2 * i]), alpha),
-                                      __fmul_rn(__uint_as_float(r[2 * i + 1]), alpha), kBF16);
+        for (int i = 0; i < 16; ++i) {
+          out[ch * 16 + i] = pack_out(__fmul_rn(__uint_as_float(r0[2 * i]), alpha),
+                                      __fmul_rn(__uint_as_float(r0[2 * i + 1]), alpha), kBF16);
+          out[ch * 16 + 16 + i] = pack_out(__fmul_rn(__uint_as_float(r1[2 * i]), alpha),
+                                           __fmul_rn(__uint_as_float(r1[2 * i + 1]), alpha), kBF16);
+        }
       }
       tc_fence_before();
       mbar_arrive_cluster(acc_empty0);
