@@ -16,6 +16,9 @@ ERR_MISALIGNED = 2
 ERR_UNSUPPORTED = 3
 ERR_CUDA = 4
 ERR_TENSOR_MAP = 5
+ERR_TOO_LARGE = 6
+
+NOALLOC_MAX_ELEMENTS = 1 << 31
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 L2_NORMAL, L2_EVICT_FIRST, L2_EVICT_LAST = 0, 1, 2
@@ -32,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_strerror",
     "nvfp4_last_cuda_error",
     "nvfp4_abi_version",
+    "nvfp4_quantize_global_noalloc",
 )
 
 
@@ -80,6 +84,7 @@ _SIGNATURES = {
     "nvfp4_strerror": (ctypes.c_char_p, [_i32]),
     "nvfp4_last_cuda_error": (_i32, []),
     "nvfp4_abi_version": (_i32, []),
+    "nvfp4_quantize_global_noalloc": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
 }
 
 

@@ -159,6 +159,7 @@ const char* nvfp4_strerror(int32_t code) {
     case NVFP4_ERR_UNSUPPORTED: return "unsupported device or feature (needs sm_100)";
     case NVFP4_ERR_CUDA: return "CUDA runtime error";
     case NVFP4_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled rejected the operand";
+    case NVFP4_ERR_TOO_LARGE: return "input larger than NVFP4_NOALLOC_MAX_ELEMENTS (2^31 elements)";
     case NVFP4_DEV_TIMEOUT_FULL: return "device timeout: MMA issuer waiting for a filled stage";
     case NVFP4_DEV_TIMEOUT_EMPTY: return "device timeout: producer waiting for a free stage";
     case NVFP4_DEV_TIMEOUT_ACC_FULL: return "device timeout: epilogue waiting for the accumulator";
@@ -435,3 +436,117 @@ int nvfp4_swizzle_sf(const void* sf_linear, int64_t rows, int64_t cols, void* ou
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Global-scale quantisation that allocates nothing.
+//
+// nvfp4_quantize with gs_mode 2 reads the tensor amax from a device float that the caller
+// allocates and nvfp4_amax fills. Some callers cannot allocate it: a plugin or custom-call hook
+// that a host framework hands only its input and output buffers, code running where cudaMalloc
+// is not allowed (it can synchronise the device, and it is not legal while the stream is being
+// captured), or a process whose memory is carved up in advance. nvfp4_quantize_global_noalloc
+// keeps that intermediate in a fixed array of this library's own device memory instead.
+namespace {
+
+// Elements reduced by one block of the first pass, and how many per-block maxima the array holds;
+// together they bound the input at 2^31 elements.
+constexpr int64_t kNoAllocChunk = 65536;
+constexpr int kNoAllocPartials = 32768;
+static_assert(kNoAllocChunk * kNoAllocPartials == NVFP4_NOALLOC_MAX_ELEMENTS, "header limit out of sync");
+
+// Words [0, kNoAllocPartials): per-block max |x| as FP32 bits; word kNoAllocPartials: the tensor
+// amax read by the quantiser. 131,328 bytes, present on every device that loads this library
+// until the process exits. Host code must not pass this name to a kernel (on the host it is only
+// a stand-in); noalloc_scratch() gets the device address.
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocPartials + 64];
+
+uint32_t* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `dev` (which must be current), looked up on the first
+// call for that device and cached.
+int noalloc_scratch(int dev, uint32_t** out) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    G3_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (p == nullptr) return NVFP4_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return NVFP4_OK;
+}
+
+// Pass 1: block b writes max |x| over elements [b * kNoAllocChunk, (b + 1) * kNoAllocChunk) to
+// partials[b] as FP32 bits (NaN bits order above +Inf, so a NaN wins, as in nvfp4_amax_kernel).
+// numel is a multiple of 16.
+template <int kInDtype>
+__global__ void __launch_bounds__(256) noalloc_partial_amax_kernel(const void* x, int64_t numel, uint32_t* partials) {
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * kNoAllocChunk;
+  const int64_t end = begin + kNoAllocChunk < numel ? begin + kNoAllocChunk : numel;
+  uint32_t m = 0;
+  for (int64_t e = begin + static_cast<int64_t>(threadIdx.x) * 16; e < end; e += 256 * 16) {
+    float v[16];
+    g3::load16<kInDtype>(x, e, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+  }
+  __shared__ uint32_t warp_max[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = max(m, warp_max[w]);
+    partials[blockIdx.x] = m;
+  }
+}
+
+// Pass 2: scratch[kNoAllocPartials] = max of the `parts` partials just written by pass 1.
+__global__ void __launch_bounds__(1024) noalloc_final_amax_kernel(uint32_t* scratch, int parts) {
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < parts; i += 1024) m = max(m, scratch[i]);
+  __shared__ uint32_t warp_max[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = warp_max[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) scratch[kNoAllocPartials] = m;
+  }
+}
+
+}  // namespace
+
+extern "C" int nvfp4_quantize_global_noalloc(const void* x, int32_t in_dtype, int64_t rows, int64_t k, void* packed,
+                                             void* sf_swizzled, void* sf_linear, float* gs_out, void* stream) {
+  if (!x || !packed || !sf_swizzled) return NVFP4_ERR_INVALID_VALUE;
+  if (rows < 1 || k < 16 || k % 16) return NVFP4_ERR_INVALID_VALUE;
+  if (in_dtype < NVFP4_DTYPE_F16 || in_dtype > NVFP4_DTYPE_F32) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(x, 16) || !aligned(packed, 8)) return NVFP4_ERR_MISALIGNED;
+  if (rows > NVFP4_NOALLOC_MAX_ELEMENTS / k) return NVFP4_ERR_TOO_LARGE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  uint32_t* scratch = nullptr;
+  rc = noalloc_scratch(dev, &scratch);
+  if (rc != NVFP4_OK) return rc;
+  // Every partial that pass 2 reads is written by pass 1 of the same call, and the amax word is
+  // written by pass 2 before the quantiser reads it, so nothing needs clearing between calls.
+  const int64_t numel = rows * k;
+  const int parts = static_cast<int>((numel + kNoAllocChunk - 1) / kNoAllocChunk);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (in_dtype) {
+    case NVFP4_DTYPE_F16: noalloc_partial_amax_kernel<0><<<parts, 256, 0, s>>>(x, numel, scratch); break;
+    case NVFP4_DTYPE_BF16: noalloc_partial_amax_kernel<1><<<parts, 256, 0, s>>>(x, numel, scratch); break;
+    default: noalloc_partial_amax_kernel<2><<<parts, 256, 0, s>>>(x, numel, scratch); break;
+  }
+  G3_CUDA(cudaGetLastError());
+  noalloc_final_amax_kernel<<<1, 1024, 0, s>>>(scratch, parts);
+  G3_CUDA(cudaGetLastError());
+  return nvfp4_quantize(x, in_dtype, rows, k, 0.0f, reinterpret_cast<const float*>(scratch + kNoAllocPartials),
+                        2, 0, packed, sf_swizzled, sf_linear, gs_out, stream);
+}

@@ -31,6 +31,7 @@ typedef enum nvfp4_status {
   NVFP4_ERR_UNSUPPORTED = 3,     /* device is not sm_100 / feature not available */
   NVFP4_ERR_CUDA = 4,            /* a CUDA runtime call failed; see nvfp4_last_cuda_error() */
   NVFP4_ERR_TENSOR_MAP = 5,      /* cuTensorMapEncodeTiled rejected the operand */
+  NVFP4_ERR_TOO_LARGE = 6,       /* input exceeds NVFP4_NOALLOC_MAX_ELEMENTS (no-allocation variant) */
   /* Device-side status words (written by kernels into the caller's int32 status buffer). */
   NVFP4_DEV_TIMEOUT_FULL = 101,
   NVFP4_DEV_TIMEOUT_EMPTY = 102,
@@ -109,6 +110,32 @@ int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, flo
  * 2688 / amax (= 1 / (amax / (6 * 448))) is derived for nvfp4_quantize gs_mode 2.
  */
 int nvfp4_amax(const void* x, int32_t in_dtype, int64_t numel, float* amax_out, void* stream);
+
+/*
+ * nvfp4_amax followed by nvfp4_quantize in gs_mode 2 (div_mode 0), without the caller-allocated
+ * amax float in between. No counterpart in the reference package.
+ *
+ * For callers that cannot allocate device memory: a plugin or custom-call hook that its host
+ * framework hands only input and output buffers, code that may not call cudaMalloc because it
+ * can synchronise the device or because a stream capture is open, or a process whose device
+ * memory is all reserved up front. The amax intermediate lives instead in a fixed array of this
+ * library's device memory (131,328 bytes, held on each device that loads the library until the
+ * process exits). Outputs are bit-identical to nvfp4_amax + nvfp4_quantize(gs_mode 2, div_mode 0);
+ * the gs used is written to gs_out when it is not NULL.
+ *
+ * - rows * k must not exceed NVFP4_NOALLOC_MAX_ELEMENTS (2^31); larger inputs return
+ *   NVFP4_ERR_TOO_LARGE before anything is launched.
+ * - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ *   that device current; make that first call before any stream capture.
+ * - Every call, on any stream, uses the same array: calls on one device whose kernels overlap on
+ *   the GPU race and give wrong scales. Order them on one stream or with events. Nothing in the
+ *   array needs to start at zero; each call writes what it reads.
+ * - Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+#define NVFP4_NOALLOC_MAX_ELEMENTS 2147483648LL
+int nvfp4_quantize_global_noalloc(const void* x, int32_t in_dtype, int64_t rows, int64_t k,
+                                  void* packed, void* sf_swizzled, void* sf_linear, float* gs_out,
+                                  void* stream);
 
 /*
  * out[rows, K] (float32) = E2M1(code) * e4m3(scale) / global_scale.
