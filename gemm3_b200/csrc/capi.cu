@@ -39,6 +39,7 @@ struct DeviceCache {
   int64_t l2_bytes = 0;
   bool gemm_attr_set = false;
   int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
+  int quant_blocks[3] = {0, 0, 0};  // co-resident 256-thread quantiser blocks per SM, per input dtype
 };
 DeviceCache g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -140,6 +141,30 @@ int encode_scales(CUtensorMap* m, const void* base, int64_t rowblocks, int64_t k
 int grid_for(int64_t work, int sm_count, int threads = 256) {
   const int64_t want = (work + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+// One full wave of the grid-stride quantiser: every SM holds as many blocks as fit, so no
+// partial second wave is left at the end.
+int quant_grid(DeviceCache* d, int32_t in_dtype, int64_t work) {
+  int& per_sm = d->quant_blocks[in_dtype];
+  if (per_sm == 0) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    int n = 0;
+    cudaError_t e = cudaSuccess;
+    switch (in_dtype) {
+      case NVFP4_DTYPE_F16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, g3::nvfp4_quantize_kernel<0>, 256, 0); break;
+      case NVFP4_DTYPE_BF16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, g3::nvfp4_quantize_kernel<1>, 256, 0); break;
+      default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, g3::nvfp4_quantize_kernel<2>, 256, 0); break;
+    }
+    if (e != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = 4;
+    }
+    per_sm = n;
+  }
+  const int64_t want = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(d->sm_count) * per_sm;
   return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
@@ -358,7 +383,7 @@ int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, flo
   p.sf_swz = static_cast<uint8_t*>(sf_swizzled);
   p.sf_lin = static_cast<uint8_t*>(sf_linear);
   p.gs_out = gs_out;
-  const int grid = grid_for(p.rows_pad * p.cols_pad, d->sm_count);
+  const int grid = quant_grid(d, in_dtype, p.rows_pad * p.cols_pad);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (in_dtype) {
     case NVFP4_DTYPE_F16: g3::nvfp4_quantize_kernel<0><<<grid, 256, 0, s>>>(p); break;

@@ -7,10 +7,23 @@
 //   q     = scale > 0 ? xb / scale : 0                      (IEEE division)
 //   code  = argmin_i (|min(|q|, 6) - E2M1[i]| + (i odd) * 1e-6f), first index on ties
 //           | 8 if q < 0                                     (quant.py:15-28)
-// The argmin runs on the two table entries that bracket |q|: the distance to every other entry
-// is larger by at least 0.5, far more than the 1e-6 penalty, and FP32 subtraction is monotone,
-// so the bracketing pair always holds the minimum. Both distances are computed with the same
-// FP32 operations as the reference (no contraction), so ties resolve identically.
+// The code is a monotone step function of |q|: the reference's FP32 distances to the two
+// bracketing table entries move in opposite directions as |q| grows, and every other entry is at
+// least 0.5 further away. So code = the number of thresholds T1..T7 that |q| reaches, where Tk is
+// the smallest float that the reference rounds to code k (found by bisection with the CPU
+// restatement and checked against it for every float in [0, 6]; |q| >= 6 clamps to code 7).
+//
+// q itself is the IEEE quotient xb / scale. A scale is an E4M3 value, so its significand is one
+// of eight values 1 + m/8. With r = the correctly rounded 1/scale (one reciprocal per block),
+// Markstein's correction  q1 = xb*r, rem = fma(-q1, scale, xb), q = fma(rem, r, q1)  returns
+// the correctly rounded quotient for all 2^23 significands of xb and all eight of the scale
+// (checked exhaustively on the CPU); exponents only shift the result while no intermediate
+// leaves the normal range, which holds for |xb| >= 2^-100. Below that |q| < 2^-91, so the
+// magnitude code is 0 however q rounds, and the sign bit is decided from xb and the scale
+// directly (e2m1_pack16).
+//
+// Per element the work is FP32 multiply-adds only (the threshold tests are saturating FMAs), so
+// the kernel is not limited by the integer/compare pipe, which has half the FMA pipe's rate.
 //
 // One thread owns one 16-element scale block. Consecutive threads own consecutive blocks of
 // the row-major input, so loads (32 or 64 bytes per thread), code stores (8 bytes) and linear
@@ -50,16 +63,62 @@ __device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
 
 __device__ __constant__ float kE2M1Table[9] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f, 6.0f};
 
-// Nearest E2M1 magnitude code (0-7) of q, with the reference's tie rule.
-__device__ __forceinline__ uint32_t e2m1_code(float q) {
-  const float mag = fminf(fabsf(q), 6.0f);  // torch clamp(max=6); NaN handled by the caller
-  const uint32_t i = (mag >= 0.5f) + (mag >= 1.0f) + (mag >= 1.5f) + (mag >= 2.0f) + (mag >= 3.0f) +
-                     (mag >= 4.0f) + (mag >= 6.0f);
-  if (i == 7u) return 7u;
-  const float pen = 9.99999997e-07f;  // float32(1e-6), added to odd codes
-  const float d_lo = __fadd_rn(__fsub_rn(mag, kE2M1Table[i]), (i & 1u) ? pen : 0.0f);
-  const float d_hi = __fadd_rn(__fsub_rn(kE2M1Table[i + 1], mag), ((i + 1u) & 1u) ? pen : 0.0f);
-  return d_hi < d_lo ? i + 1u : i;
+// Smallest FP32 |q| (as bits) that the reference rounds to E2M1 codes 1..7 (quant.py:15-28): the
+// midpoints 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5 moved by the 1e-6 penalty on odd codes.
+constexpr uint32_t kE2M1T1 = 0x3E800012u, kE2M1T2 = 0x3F3FFFF8u, kE2M1T3 = 0x3FA00005u, kE2M1T4 = 0x3FDFFFFCu,
+                   kE2M1T5 = 0x40200003u, kE2M1T6 = 0x405FFFFEu, kE2M1T7 = 0x40A00002u;
+
+// d = sat(a * b + c) and d = sat(a * b), one rounding each; sat clamps to [0, 1] (NaN -> 0).
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+  float d;
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float mul_sat(float a, float b) {
+  float d;
+  asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// Packed E2M1 codes of the sixteen quotients xb[i] / d (d > 0 finite, r = the correctly rounded
+// 1 / d): nibble i of the 64-bit result, sign in bit 3. All arithmetic is exact FP32 on the FMA
+// pipe, so the integer/compare pipe stays free:
+//  - magnitude: with P = the float below T, the step sat(|q| * 2^100 - P * 2^100) is exactly 1
+//    when |q| >= T (the difference is at least one ulp, 2^-25, so the product is >= 2^75) and
+//    exactly 0 otherwise; the code is the sum of the seven steps;
+//  - sign: q = RN(xb / d) < 0 exactly when xb / d < -2^-150 (the tie at 2^-150 rounds to -0),
+//    i.e. when -xb * 2^100 - d * 2^-50 > 0; both products are exact and the FMA keeps the sign,
+//    and any positive result is a multiple of 2^-73, so multiplying by 2^127 and saturating
+//    gives exactly 1. Tiny xb therefore needs no division: its magnitude code is 0 whatever
+//    rounding the quotient sees, and its sign comes from xb and d directly;
+//  - the sum starts at 2^23, so the float's low mantissa bits are the code; the words are built
+//    with integer multiply-adds and the 2^23 bias (0x4B000000 per nibble) removed at the end.
+__device__ __forceinline__ uint2 e2m1_pack16(const float (&xb)[16], float d, float r) {
+  const float nd = -d;
+  const float d_lo = __fmul_rn(d, 0x1p-50f);
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float q1 = __fmul_rn(xb[i], r);
+    const float rem = __fmaf_rn(q1, nd, xb[i]);
+    const float mag = fabsf(__fmaf_rn(rem, r, q1));
+    const float neg = mul_sat(__fmaf_rn(-xb[i], 0x1p100f, -d_lo), 0x1p127f);
+    float acc = __fmaf_rn(neg, 8.0f, 8388608.0f);
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.000022p+98f));  // T1 0x3E800012
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.7fffeep+99f));  // T2 0x3F3FFFF8
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400008p+100f)); // T3 0x3FA00005
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffff6p+100f)); // T4 0x3FDFFFFC
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400004p+101f)); // T5 0x40200003
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffffap+101f)); // T6 0x405FFFFE
+    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400002p+102f)); // T7 0x40A00002
+    const uint32_t bits = __float_as_uint(acc);  // 0x4B000000 + code
+    if (i < 8)
+      w0 += bits * (1u << (4 * i));
+    else
+      w1 += bits * (1u << (4 * (i - 8)));
+  }
+  // sum over nibbles of 0x4B000000 << 4i, modulo 2^32
+  return make_uint2(w0 - 0xFB000000u, w1 - 0xFB000000u);
 }
 
 // Byte offset of scale (row, col) in the 128x4 swizzled layout with `c4` 4-column groups.
@@ -129,40 +188,40 @@ __global__ void __launch_bounds__(256) nvfp4_quantize_kernel(const QuantParams p
   const float inv6 = 0.166666672f;  // fl(1/6): what torch on CUDA multiplies by for "/ 6.0"
   const int64_t total = p.rows_pad * p.cols_pad;
   const int64_t c4 = p.cols_pad >> 2;
-  for (int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; b < total;
-       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = b / p.cols_pad;
-    const int64_t c = b - r * p.cols_pad;
+  // Block (r, c) of the padded scale grid, advanced by the grid stride without dividing.
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t dr = stride / p.cols_pad, dc = stride - dr * p.cols_pad;
+  int64_t r = b0 / p.cols_pad, c = b0 - r * p.cols_pad;
+  for (int64_t b = b0; b < total; b += stride) {
     uint32_t sf = 0;
     if (r < p.rows && c < p.cols) {
       float v[16];
       load16<kInDtype>(p.x, r * p.k + c * 16, v);
-      float amax = 0.0f;
-      bool nan = false;
+      // amax over finite values; `inf_nan` becomes NaN if any element is Inf or NaN (x * 0). The
+      // reference's scale is then NaN either way (NaN amax, or Inf / 6 overflowing E4M3).
+      float amax = 0.0f, inf_nan = 0.0f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         v[i] = __fmul_rn(v[i], gs);
-        const float a = fabsf(v[i]);
-        nan |= (a != a);
-        amax = fmaxf(amax, a);
+        amax = fmaxf(amax, fabsf(v[i]));
+        inf_nan = __fmaf_rn(v[i], 0.0f, inf_nan);
       }
       const float s = p.div_mode == 0 ? __fmul_rn(amax, inv6) : __fdiv_rn(amax, 6.0f);
-      sf = nan ? 0x7Fu : f32_to_e4m3_rn(s);
+      sf = inf_nan != 0.0f ? 0x7Fu : f32_to_e4m3_rn(s);
       const float denom = e4m3_to_f32(sf);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float q = denom > 0.0f ? __fdiv_rn(v[i], denom) : 0.0f;
-        const uint32_t code = e2m1_code(q) | (q < 0.0f ? 8u : 0u);
-        if (i < 8)
-          lo |= code << (4 * i);
-        else
-          hi |= code << (4 * (i - 8));
-      }
-      *reinterpret_cast<uint2*>(p.packed + r * (p.k >> 1) + c * 8) = make_uint2(lo, hi);
+      // else q = 0 for every element: code 0 (a NaN scale included)
+      const uint2 codes = denom > 0.0f ? e2m1_pack16(v, denom, __frcp_rn(denom)) : make_uint2(0u, 0u);
+      *reinterpret_cast<uint2*>(p.packed + r * (p.k >> 1) + c * 8) = codes;
       if (p.sf_lin != nullptr) p.sf_lin[r * p.cols + c] = static_cast<uint8_t>(sf);
     }
     p.sf_swz[sf_swizzle_offset(r, c, c4)] = static_cast<uint8_t>(sf);
+    c += dc;
+    r += dr;
+    if (c >= p.cols_pad) {
+      c -= p.cols_pad;
+      ++r;
+    }
   }
 }
 

@@ -1,0 +1,78 @@
+"""CPU: the two arithmetic identities the GPU quantiser relies on, pinned against the reference
+restatement (oracle/) and against IEEE division.
+
+1. The E2M1 code of q (quant.py:15-28) is the number of thresholds T1..T7 that |q| reaches.
+   The thresholds in csrc/quant_kernel.cuh are re-derived here by bisection with the oracle and
+   checked on windows around each of them and on a strided sweep of [0, 6].
+2. Markstein's correction with a correctly rounded reciprocal reproduces x / d exactly for every
+   E4M3 divisor significand (an exhaustive C check).
+"""
+
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+KERNEL = os.path.join(REPO, "gemm3_b200", "csrc", "quant_kernel.cuh")
+TABLE = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+
+
+def kernel_thresholds():
+    text = open(KERNEL).read()
+    found = dict(re.findall(r"kE2M1T(\d) = (0x[0-9A-Fa-f]+)u", text))
+    assert sorted(found) == [str(i) for i in range(1, 8)]
+    return np.array([int(found[str(i)], 16) for i in range(1, 8)], dtype=np.uint32)
+
+
+def oracle_codes(bits):
+    return oracle.e2m1_code(np.asarray(bits, dtype=np.uint32).view(np.float32))
+
+
+def test_thresholds_are_the_oracles_rounding_boundaries():
+    want = []
+    for i in range(7):
+        lo = int(np.float32(TABLE[i]).view(np.uint32))
+        hi = int(np.float32(TABLE[i + 1]).view(np.uint32))
+        assert oracle_codes([lo])[0] == i and oracle_codes([hi])[0] == i + 1
+        while hi - lo > 1:  # smallest float in (lo, hi] with code i + 1
+            mid = (lo + hi) // 2
+            if oracle_codes([mid])[0] == i + 1:
+                hi = mid
+            else:
+                lo = mid
+        want.append(hi)
+    np.testing.assert_array_equal(kernel_thresholds(), np.array(want, dtype=np.uint32))
+
+
+def test_step_constants_are_scaled_predecessors():
+    """e2m1_pack16 subtracts P * 2^100 for P = the float just below each threshold."""
+    text = open(KERNEL).read()
+    lits = re.findall(r"fma_sat\(mag, 0x1p100f, -(0x[0-9a-f.]+p\+\d+)f\)\);\s*// T(\d) (0x[0-9A-F]+)", text)
+    assert [int(k) for _, k, _ in lits] == list(range(1, 8))
+    t = kernel_thresholds()
+    for (lit, k, tbits), want in zip(lits, t):
+        assert int(tbits, 16) == int(want)
+        pred = np.uint32(int(want) - 1).view(np.float32)
+        assert float.fromhex(lit) == float(pred) * 2.0**100, (k, lit)
+
+
+def test_threshold_count_matches_oracle_codes():
+    t = kernel_thresholds()
+    windows = [np.arange(int(x) - 65536, int(x) + 65536, dtype=np.uint32) for x in t]
+    sweep = np.arange(0, int(np.float32(6.0).view(np.uint32)) + 1, 257, dtype=np.uint32)
+    above = np.float32([6.0, 6.5, 100.0, 3.0e38]).view(np.uint32)
+    bits = np.concatenate(windows + [sweep, above])
+    np.testing.assert_array_equal(np.searchsorted(t, bits, side="right"), oracle_codes(bits))
+
+
+def test_markstein_quotient_is_exact(tmp_path):
+    src = os.path.join(REPO, "tests", "c", "markstein_check.c")
+    exe = str(tmp_path / "markstein_check")
+    subprocess.run(["gcc", "-O2", "-ffp-contract=off", "-o", exe, src, "-lm"], check=True)
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0 and res.stdout.strip() == "0", res.stdout

@@ -83,6 +83,42 @@ def test_quantize_global_scale_on_device(cuda_ext):
     assert torch.equal(p2, packed) and torch.equal(s2, sf_swz)
 
 
+def _boundary_blocks():
+    """16-element FP32 blocks whose first element 6*d pins the block scale to the E4M3 value d;
+    the other 15 are dividends within 24 ulps of d times each E2M1 rounding midpoint (and of
+    their negatives), for every E4M3 significand at several exponents, including subnormal
+    scales; plus blocks of zeros, signed zeros and tiny values next to a large scale."""
+    blocks = []
+    for e in (-9, -7, -6, -3, 0, 4, 7, 8):
+        for m in range(8):
+            d = np.float32((1.0 + m / 8.0) * 2.0**e)
+            if d > 448.0 or (e < -6 and m != 0):
+                continue
+            for mid in (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0):
+                base = int(np.float32(np.float32(mid) * d).view(np.uint32))
+                vals = (np.arange(base - 24, base + 24, dtype=np.int64).astype(np.uint32)).view(np.float32)
+                vals = np.concatenate([vals, -vals])
+                for i in range(0, len(vals) - 14, 15):
+                    blocks.append(np.concatenate([[6.0 * d], vals[i:i + 15]]).astype(np.float32))
+    tiny = np.float32([0.0, -0.0, 1e-45, -1e-45, 1e-40, -1e-38, 2.0**-101, -(2.0**-100), 2.0**-99, -1e-30,
+                       3e-39, -3e-39, 0.0, -0.0, 7.0e-44])
+    for d in (np.float32(448.0), np.float32(1.0), np.float32(2.0**-9)):
+        blocks.append(np.concatenate([[6.0 * d], tiny]).astype(np.float32))
+    while len(blocks) % 4:
+        blocks.append(np.zeros(16, np.float32))
+    return np.stack(blocks).reshape(-1, 64)
+
+
+def test_quantize_near_rounding_boundaries(cuda_ext):
+    """Division shortcut and threshold codes against the oracle's IEEE division and argmin."""
+    x = _boundary_blocks()
+    packed, sf_swz, sf_lin = cuda_ext.quantize_nvfp4(torch.from_numpy(x).cuda(), 1.0)
+    want = oracle.quantize(x, 1.0, div_mode=0)
+    np.testing.assert_array_equal(sf_lin.cpu().numpy(), want[2])
+    np.testing.assert_array_equal(packed.cpu().numpy(), want[0])
+    np.testing.assert_array_equal(sf_swz.cpu().numpy(), want[1])
+
+
 def test_amax_odd_sizes_and_nan(cuda_ext):
     for n in (1, 15, 16, 17, 1000003):
         x = torch.randn(n, device="cuda")
