@@ -172,6 +172,26 @@ def run_reference(args):
     return 0
 
 
+def profiled_traffic(m, n, k, out_dtype):
+    """DRAM bytes (read + write) of one GEMM kernel launch of this shape, from the ncu summaries
+    committed under profiles/: a file with the lines `shape: <M>x<N>x<K> <bf16|fp16>` and
+    `traffic_bytes_per_launch: <int>`. None when no capture covers the shape."""
+    import glob
+
+    want = f"{m}x{n}x{k} {out_dtype}"
+    for path in sorted(glob.glob(os.path.join(REPO, "profiles", "*"))):
+        shape = traffic = None
+        with open(path) as f:
+            for line in f:
+                if line.startswith("shape: "):
+                    shape = line.split(":", 1)[1].strip()
+                elif line.startswith("traffic_bytes_per_launch: "):
+                    traffic = int(line.split(":", 1)[1].strip())
+        if shape == want and traffic:
+            return traffic
+    return None
+
+
 def workload_config(args):
     return {
         "workload": f"NVFP4 GEMM {args.size}x{args.size * args.gpus}x{args.size} "
@@ -394,7 +414,8 @@ def run_ours(args):
             "peak_source": (f"4 x bf16_tflops of MEASURED_PEAKS.json ({bf16_peak:.0f}); dense FP4 = 4x dense BF16"
                             if peak_src == "measured" else f"4 x fallback bf16 {bf16_peak:.0f}"),
             "frac_of_nominal_9pf": achieved / NOMINAL_FP4_DENSE_TFLOPS,
-            "traffic": None,
+            "traffic": profiled_traffic(M, N, K, args.out_dtype),
+            "algorithmic_bytes": M * K // 2 + N * K // 2 + (M + N) * K // 16 + 2 * M * N,
         },
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
