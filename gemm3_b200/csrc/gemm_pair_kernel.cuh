@@ -50,9 +50,9 @@ constexpr int kPairOffB = kPairOffA + kPairStages * kPairABytes;
 constexpr int kPairOffSfa = kPairOffB + kPairStages * kPairBBytes;
 constexpr int kPairOffSfb = kPairOffSfa + kPairSfSlots * kPairSfaBytes;
 constexpr int kPairOffBar = kPairOffSfb + kPairSfSlots * kPairSfbBytes;
-// full[S], empty[S], sfa_ready[S], sfb_ready[S], sf_full[Q], sf_empty[Q], acc_full, acc_empty,
-// drain[3] (one per tcgen05 issuer)
-constexpr int kPairNumBars = 4 * kPairStages + 2 * kPairSfSlots + 5;
+// full[S], empty[S], ready[S], sf_full[Q], sf_empty[Q], acc_full, acc_empty, drain[3] (one per
+// tcgen05 issuer)
+constexpr int kPairNumBars = 3 * kPairStages + 2 * kPairSfSlots + 5;
 constexpr int kPairThreads = 288;
 constexpr int kPairOffTmemSlot = kPairOffBar + kPairNumBars * 8;
 constexpr int kPairOffAbort = kPairOffTmemSlot + 4;
@@ -74,9 +74,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBar);
   uint64_t* full = bars;
   uint64_t* empty = full + kPairStages;
-  uint64_t* sfa_ready = empty + kPairStages;
-  uint64_t* sfb_ready = sfa_ready + kPairStages;
-  uint64_t* sf_full = sfb_ready + kPairStages;
+  uint64_t* ready = empty + kPairStages;  // stage's scales copied and its A/B data landed
+  uint64_t* sf_full = ready + kPairStages;
   uint64_t* sf_empty = sf_full + kPairSfSlots;
   uint64_t* acc_full = sf_empty + kPairSfSlots;
   uint64_t* acc_empty = acc_full + 1;
@@ -95,12 +94,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&full[s], 1);   // one arrive.expect_tx by CTA 0's A/B producer + both CTAs' bytes
       mbar_init(&empty[s], 1);  // one commit from CTA 0's MMA thread
-      mbar_init(&sfa_ready[s], 1);
-      mbar_init(&sfb_ready[s], 1);
+      mbar_init(&ready[s], 2);  // one arrive from each copy warp
     }
     for (int q = 0; q < kPairSfSlots; ++q) {
       mbar_init(&sf_full[q], 1);   // one arrive.expect_tx by CTA 0's scale producer
-      mbar_init(&sf_empty[q], 2);  // one commit from each copy warp
+      mbar_init(&sf_empty[q], 2);  // one commit from each copy warp (multicast to both CTAs)
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 4 * 32);  // every epilogue thread of both CTAs
@@ -230,8 +228,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     // ------------------------------------------------------------------ MMA issuer (CTA 0, one thread)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = idesc_nvf4(kPairTileM, kPairTileN);
-      const uint32_t empty_self = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), 1);
-      const uint32_t accf_self = smem_u32(acc_full), accf_peer = mapa_shared(smem_u32(acc_full), 1);
+      const uint32_t empty_off = smem_u32(empty), accf_off = smem_u32(acc_full);
       uint32_t stage = 0, phase = 0, acc_phase = 0;
       bool ok = true;
       for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
@@ -241,9 +238,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         tc_fence_after();
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!mbar_wait(&sfa_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag) ||
-              !mbar_wait(&sfb_ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag) ||
-              !mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+          if (!mbar_wait(&ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
             ok = false;
             break;
           }
@@ -263,16 +258,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
                                (kt | j) != 0 ? 1u : 0u);
           }
-          tc_commit_pair(empty_self + 8u * stage);
-          tc_commit_pair(empty_peer + 8u * stage);
+          tc_commit_pair_mc(empty_off + 8u * stage, 0x3);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(accf_self);
-        tc_commit_pair(accf_peer);
+        tc_commit_pair_mc(accf_off, 0x3);
         acc_phase ^= 1u;
       }
       if (!ok) {
@@ -289,8 +282,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     // readers of that region, have completed.
     if (leader && lane == 0) {
       const bool is_a = warp == 3;
-      uint64_t* ready = is_a ? sfa_ready : sfb_ready;
-      const uint32_t sfe_self = smem_u32(sf_empty), sfe_peer = mapa_shared(smem_u32(sf_empty), 1);
+      const uint32_t sfe_off = smem_u32(sf_empty);
       uint32_t stage = 0, phase = 0, slot = 0, sphase = 0;
       bool ok = true;
       for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
@@ -329,12 +321,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           // The TMEM region goes to the MMA thread as soon as the copies are issued: the fence
           // orders them before this arrive, the MMA thread's after_thread_sync fence orders its
-          // MMAs after it, and the tensor pipe runs them in that order. The shared-memory slot
-          // is freed only when the copies have completed.
+          // MMAs after it, and the tensor pipe runs them in that order. Warp 3 also waits for the
+          // stage's A/B data, so the MMA thread waits on one barrier per k-tile. The
+          // shared-memory slot is freed only when the copies have completed.
           tc_fence_before();
+          if (is_a && !mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
           mbar_arrive(&ready[stage]);
-          tc_commit_pair(sfe_self + 8u * slot);
-          tc_commit_pair(sfe_peer + 8u * slot);
+          tc_commit_pair_mc(sfe_off + 8u * slot, 0x3);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1u;

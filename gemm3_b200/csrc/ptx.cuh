@@ -313,6 +313,15 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
                : "memory");
 }
 
+// One arrive, when this thread's earlier tcgen05 operations have completed, on the mbarrier at
+// shared-memory offset `bar` of every CTA of the cluster in `cta_mask` (bit r = rank r).
+__device__ __forceinline__ void tc_commit_pair_mc(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // Scale chunk copy into both CTAs' TMEM, each from its own shared memory at the same offset.
 __device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
