@@ -11,19 +11,21 @@
 // TMEM are issued before the A/B data of the same k-tile lands and stay off the critical path.
 // Scales sit in TMEM in one 48-column region per A/B stage.
 //
-// Roles (per CTA, 9 warps):
+// Roles (per CTA, 10 warps):
 //   warp 0      A/B producer, both CTAs: TMA loads of its A and B halves (128 rows x 128 B,
 //               128-byte swizzle), completing on CTA 0's "full" barrier of the stage;
 //   warp 2      scale producer, both CTAs: TMA loads of its 128 rows of A scales and all 256 rows
 //               of B scales (3-D tensor maps over the swizzled layout), on CTA 0's "sf_full";
 //   warp 1      TMEM owner in both CTAs; in CTA 0 the MMA issuer: one tcgen05.mma (cta_group::2)
-//               per 64-element block; commits release the A/B stage in both CTAs and, per tile,
-//               hand the accumulator to both epilogues;
-//   warps 3, 4  in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 3 one
-//               A-scale chunk per 64-element block, warp 4 the two B-scale chunks. Every tcgen05
-//               instruction costs its issuing thread ~50 cycles, so the three copies and the MMA
-//               of a block are spread over three threads. A copy warp hands its TMEM region to the
-//               MMA thread once the copies are issued (fence + mbarrier arrive) and frees the
+//               per 64-element block after one wait per k-tile; one multicast commit releases the
+//               A/B stage in both CTAs and, per tile, hands the accumulator to both epilogues;
+//   warps 3,4,9 in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 3 one
+//               A-scale chunk per 64-element block, warps 4 and 9 the B-scale chunks of tile
+//               rows 0-127 and 128-255. Every tcgen05 instruction costs its issuing thread about
+//               50 cycles, so the three copies and the MMA of a block are spread over four
+//               threads (with one thread for both B chunks, that thread set the pace). A copy
+//               warp hands its TMEM region to the MMA thread once the copies are issued (fence +
+//               mbarrier arrive; warp 3 first waits for the stage's A/B data) and frees the
 //               shared-memory slot through a commit when they have completed;
 //   warps 5-8   epilogue, both CTAs: TMEM -> registers -> x alpha -> FP16/BF16, accumulator
 //               released to CTA 0's MMA warp, then 256-bit row stores.
@@ -50,10 +52,11 @@ constexpr int kPairOffB = kPairOffA + kPairStages * kPairABytes;
 constexpr int kPairOffSfa = kPairOffB + kPairStages * kPairBBytes;
 constexpr int kPairOffSfb = kPairOffSfa + kPairSfSlots * kPairSfaBytes;
 constexpr int kPairOffBar = kPairOffSfb + kPairSfSlots * kPairSfbBytes;
-// full[S], empty[S], ready[S], sf_full[Q], sf_empty[Q], acc_full, acc_empty, drain[3] (one per
+// full[S], empty[S], ready[S], sf_full[Q], sf_empty[Q], acc_full, acc_empty, drain[4] (one per
 // tcgen05 issuer)
-constexpr int kPairNumBars = 3 * kPairStages + 2 * kPairSfSlots + 5;
-constexpr int kPairThreads = 288;
+constexpr int kPairNumBars = 3 * kPairStages + 2 * kPairSfSlots + 6;
+constexpr int kPairCopyWarps = 3;  // A scales, B scales rows 0-127, B scales rows 128-255
+constexpr int kPairThreads = 320;
 constexpr int kPairOffTmemSlot = kPairOffBar + kPairNumBars * 8;
 constexpr int kPairOffAbort = kPairOffTmemSlot + 4;
 constexpr int kPairSmemBytes = kPairOffAbort + 4 + 1024;
@@ -79,7 +82,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* sf_empty = sf_full + kPairSfSlots;
   uint64_t* acc_full = sf_empty + kPairSfSlots;
   uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_full + 2;  // [0] MMA, [1] A scales, [2] B scales
+  uint64_t* drain = acc_full + 2;  // [0] MMA, [1] A scales, [2] B scales 0-127, [3] B scales 128-255
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairOffAbort);
 
@@ -94,15 +97,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&full[s], 1);   // one arrive.expect_tx by CTA 0's A/B producer + both CTAs' bytes
       mbar_init(&empty[s], 1);  // one commit from CTA 0's MMA thread
-      mbar_init(&ready[s], 2);  // one arrive from each copy warp
+      mbar_init(&ready[s], kPairCopyWarps);  // one arrive from each copy warp
     }
     for (int q = 0; q < kPairSfSlots; ++q) {
       mbar_init(&sf_full[q], 1);   // one arrive.expect_tx by CTA 0's scale producer
-      mbar_init(&sf_empty[q], 2);  // one commit from each copy warp (multicast to both CTAs)
+      mbar_init(&sf_empty[q], kPairCopyWarps);  // one commit from each copy warp (multicast to both CTAs)
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 4 * 32);  // every epilogue thread of both CTAs
-    for (int d = 0; d < 3; ++d) mbar_init(&drain[d], 1);
+    for (int d = 0; d < 1 + kPairCopyWarps; ++d) mbar_init(&drain[d], 1);
     *abort_flag = 0;
     fence_mbarrier_init();
     prefetch_tmap(&tmap_a);
@@ -274,14 +277,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 3 || warp == 4) {
+  } else if (warp == 3 || warp == 4 || warp == 9) {
     // ------------------------------------------------------------------ scale copies (CTA 0)
-    // Warp 3 copies the A scales (one 512-byte chunk per 64-element block), warp 4 the B scales
-    // (two chunks per block, tile rows 0-127 and 128-255). K-tile g lands in scale slot g % 8 and
+    // Warp 3 copies the A scales (one 512-byte chunk per 64-element block), warps 4 and 9 the B
+    // scales of tile rows 0-127 and 128-255. K-tile g lands in scale slot g % 8 and
     // is copied into the TMEM region of A/B stage g % 5 once the MMAs of k-tile g - 5, the last
     // readers of that region, have completed.
     if (leader && lane == 0) {
       const bool is_a = warp == 3;
+      const int half = warp == 9 ? 1 : 0;  // B-scale copy warps: which 128 rows of the tile
+      const int role = is_a ? 1 : 2 + half;  // drain barrier index
       const uint32_t sfe_off = smem_u32(sf_empty);
       uint32_t stage = 0, phase = 0, slot = 0, sphase = 0;
       bool ok = true;
@@ -305,18 +310,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
             }
           } else {
-            const uint64_t dsb = sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + slot * kPairSfbBytes));
+            const uint64_t dsb =
+                sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + slot * kPairSfbBytes)) + 32 * kKBlocksPerTile * half;
+            const uint32_t tb = tsfb + 4 * half;
             if (nkb == kKBlocksPerTile) {
 #pragma unroll
-              for (int j = 0; j < kKBlocksPerTile; ++j) {
-                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
-                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
-              }
+              for (int j = 0; j < kKBlocksPerTile; ++j) tc_cp_32x128b_warpx4_pair(tb + 8 * j, dsb + 32 * j);
             } else {
-              for (int j = 0; j < nkb; ++j) {
-                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j, dsb + 32 * j);
-                tc_cp_32x128b_warpx4_pair(tsfb + 8 * j + 4, dsb + 32 * (j + kKBlocksPerTile));
-              }
+              for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4_pair(tb + 8 * j, dsb + 32 * j);
             }
           }
           // The TMEM region goes to the MMA thread as soon as the copies are issued: the fence
@@ -342,8 +343,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
       if (!ok) {
-        tc_commit_pair(smem_u32(&drain[warp - 2]));
-        mbar_wait(&drain[warp - 2], 0, p.status, kStatusTimeoutDrain, nullptr);
+        tc_commit_pair(smem_u32(&drain[role]));
+        mbar_wait(&drain[role], 0, p.status, kStatusTimeoutDrain, nullptr);
       }
     }
     __syncwarp();
