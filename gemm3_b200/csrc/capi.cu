@@ -126,11 +126,12 @@ int ensure_gemm_attributes(DeviceCache* d) {
 }
 
 // 3-D uint32 view of a swizzled scale tensor: {128 words = one 512-byte chunk, 64-element block,
-// 128-row block}; boxes of `box_rb` row blocks x 4 blocks. Out-of-range blocks read as zero.
+// 128-row block}; boxes of `box_rb` row blocks x one pair-kernel stage of blocks. Out-of-range
+// blocks read as zero.
 int encode_scales(CUtensorMap* m, const void* base, int64_t rowblocks, int64_t kblocks, uint32_t box_rb) {
   cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(kblocks), static_cast<cuuint64_t>(rowblocks)};
   cuuint64_t strides[2] = {512, static_cast<cuuint64_t>(kblocks) * 512};
-  cuuint32_t box[3] = {128, static_cast<cuuint32_t>(g3::kKBlocksPerTile), box_rb};
+  cuuint32_t box[3] = {128, static_cast<cuuint32_t>(g3::kPairKBlocks), box_rb};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,

@@ -6,10 +6,12 @@
 // CTA's half of the accumulator into its own TMEM. Compared with one-CTA 128x256 tiles this halves
 // the B bytes every SM loads from L2 and reads from shared memory per FLOP.
 //
-// Two shared-memory rings feed the MMA: a 5-stage ring of A/B k-tiles (32 KiB per CTA per stage)
-// and an 8-slot ring of scale k-tiles (6 KiB). The scale ring runs ahead, so the scale copies into
-// TMEM are issued before the A/B data of the same k-tile lands and stay off the critical path.
-// Scales sit in TMEM in one 48-column region per A/B stage.
+// A stage covers K = 512 (eight 64-element blocks, eight MMAs): the single MMA-issuing thread
+// spends about 80 cycles per tcgen05 instruction plus a few hundred per stage on its wait, fence
+// and commit, against 128 cycles of tensor-pipe time per MMA, so the per-stage work has to be
+// spread over eight MMAs to keep the pipe fed. Two shared-memory rings feed the MMA: a 3-stage
+// ring of A/B stages (64 KiB per CTA) and a 2-slot ring of scale stages (12 KiB). Scales sit in
+// TMEM in two 96-column regions used alternately, independent of the A/B stage.
 //
 // Roles (per CTA, 10 warps):
 //   warp 0      A/B producer, both CTAs: TMA loads of its A and B halves (128 rows x 128 B,
@@ -17,7 +19,7 @@
 //   warp 2      scale producer, both CTAs: TMA loads of its 128 rows of A scales and all 256 rows
 //               of B scales (3-D tensor maps over the swizzled layout), on CTA 0's "sf_full";
 //   warp 1      TMEM owner in both CTAs; in CTA 0 the MMA issuer: one tcgen05.mma (cta_group::2)
-//               per 64-element block after one wait per k-tile; one multicast commit releases the
+//               per 64-element block after one wait per stage; one multicast commit releases the
 //               A/B stage in both CTAs and, per tile, hands the accumulator to both epilogues;
 //   warps 3,4,9 in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 3 one
 //               A-scale chunk per 64-element block, warps 4 and 9 the B-scale chunks of tile
@@ -38,12 +40,16 @@ namespace g3 {
 
 constexpr int kPairTileM = 256;
 constexpr int kPairTileN = 256;
-constexpr int kPairStages = 5;    // A/B ring
-constexpr int kPairSfSlots = 8;   // scale ring
-constexpr int kPairABytes = 128 * kTileKBytes;                 // this CTA's 128 A rows
-constexpr int kPairBBytes = 128 * kTileKBytes;                 // this CTA's 128 B rows
-constexpr int kPairSfaBytes = kKBlocksPerTile * kSfChunk;      // 128 rows x 16 scales
-constexpr int kPairSfbBytes = 2 * kKBlocksPerTile * kSfChunk;  // 256 rows x 16 scales
+constexpr int kPairKBlocks = 8;                                // 64-element blocks per stage: K = 512
+constexpr int kPairKAtoms = kPairKBlocks / kKBlocksPerTile;    // 128-byte swizzle atoms per row (2)
+constexpr int kPairStages = 3;     // A/B ring
+constexpr int kPairSfSlots = 2;    // scale ring
+constexpr int kPairSfRegions = 2;  // TMEM scale regions
+constexpr int kPairAtomBytes = 128 * kTileKBytes;              // 128 rows x 128 bytes
+constexpr int kPairABytes = kPairKAtoms * kPairAtomBytes;      // this CTA's 128 A rows
+constexpr int kPairBBytes = kPairKAtoms * kPairAtomBytes;      // this CTA's 128 B rows
+constexpr int kPairSfaBytes = kPairKBlocks * kSfChunk;         // 128 rows x 32 scales
+constexpr int kPairSfbBytes = 2 * kPairKBlocks * kSfChunk;     // 256 rows x 32 scales
 constexpr uint32_t kPairAbTx = 2u * (kPairABytes + kPairBBytes);     // both CTAs, on CTA 0's barrier
 constexpr uint32_t kPairSfTx = 2u * (kPairSfaBytes + kPairSfbBytes);
 
@@ -61,10 +67,10 @@ constexpr int kPairOffTmemSlot = kPairOffBar + kPairNumBars * 8;
 constexpr int kPairOffAbort = kPairOffTmemSlot + 4;
 constexpr int kPairSmemBytes = kPairOffAbort + 4 + 1024;
 
-// TMEM columns: accumulator [0, 256); per A/B stage 16 A-scale + 32 B-scale columns.
+// TMEM columns: accumulator [0, 256); two scale regions of 32 A-scale + 64 B-scale columns.
 constexpr int kPairSfaCol = 256;
-constexpr int kPairSfColsPerStage = 4 * kKBlocksPerTile + 8 * kKBlocksPerTile;
-static_assert(kPairSfaCol + kPairStages * kPairSfColsPerStage <= kTmemCols, "pair scales do not fit in TMEM");
+constexpr int kPairSfColsPerStage = 4 * kPairKBlocks + 8 * kPairKBlocks;
+static_assert(kPairSfaCol + kPairSfRegions * kPairSfColsPerStage <= kTmemCols, "pair scales do not fit in TMEM");
 static_assert(kPairSmemBytes <= 232448, "pair kernel exceeds shared memory");
 
 template <bool kBF16>
@@ -88,6 +94,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int k_iters = (p.sf_kblocks + kPairKBlocks - 1) / kPairKBlocks;  // stages per tile
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1;
@@ -141,7 +148,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         tile_coord(p, t, mt, nt);
         const int row_a = mt * kPairTileM + 128 * static_cast<int>(rank);
         const int row_b = nt * kPairTileN + 128 * static_cast<int>(rank);
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+        for (int kt = 0; kt < k_iters; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
             ok = false;
             break;
@@ -150,12 +157,21 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full[stage], kPairAbTx);
           uint8_t* sa = smem + kPairOffA + stage * kPairABytes;
           uint8_t* sb = smem + kPairOffB + stage * kPairBBytes;
+          // one 128-byte swizzle atom (256 elements of K) per box; the stage holds kPairKAtoms
+          const int x0 = kt * kPairKAtoms * kTileKBytes;
           if (p.tma_b_first) {
-            tma_load_2d_pair(sb, &tmap_b, kt * kTileKBytes, row_b, bar, pol_b);
-            tma_load_2d_pair(sa, &tmap_a, kt * kTileKBytes, row_a, bar, pol_a);
+#pragma unroll
+            for (int h = 0; h < kPairKAtoms; ++h)
+              tma_load_2d_pair(sb + h * kPairAtomBytes, &tmap_b, x0 + h * kTileKBytes, row_b, bar, pol_b);
+#pragma unroll
+            for (int h = 0; h < kPairKAtoms; ++h)
+              tma_load_2d_pair(sa + h * kPairAtomBytes, &tmap_a, x0 + h * kTileKBytes, row_a, bar, pol_a);
           } else {
-            tma_load_2d_pair(sa, &tmap_a, kt * kTileKBytes, row_a, bar, pol_a);
-            tma_load_2d_pair(sb, &tmap_b, kt * kTileKBytes, row_b, bar, pol_b);
+#pragma unroll
+            for (int h = 0; h < kPairKAtoms; ++h) {
+              tma_load_2d_pair(sa + h * kPairAtomBytes, &tmap_a, x0 + h * kTileKBytes, row_a, bar, pol_a);
+              tma_load_2d_pair(sb + h * kPairAtomBytes, &tmap_b, x0 + h * kTileKBytes, row_b, bar, pol_b);
+            }
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -193,7 +209,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         int mt, nt;
         tile_coord(p, t, mt, nt);
         const int rb_a = (mt * kPairTileM + 128 * static_cast<int>(rank)) >> 7;
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+        for (int kt = 0; kt < k_iters; ++kt) {
           if (!mbar_wait(&sf_empty[slot], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
             ok = false;
             break;
@@ -201,7 +217,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint32_t bar = sf_full0 + 8u * slot;
           if (leader) mbar_arrive_expect_tx(&sf_full[slot], kPairSfTx);
           // scale chunks: {512-byte chunk, 64-element block, 128-row block}
-          const int kb0 = kKBlocksPerTile * kt;
+          const int kb0 = kPairKBlocks * kt;
           tma_load_3d_pair(smem + kPairOffSfa + slot * kPairSfaBytes, &tmap_sfa, 0, kb0, rb_a, bar, pol_sfa);
           tma_load_3d_pair(smem + kPairOffSfb + slot * kPairSfbBytes, &tmap_sfb, 0, kb0, 2 * nt, bar, pol_sfb);
           issued_mask |= 1u << slot;
@@ -232,7 +248,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = idesc_nvf4(kPairTileM, kPairTileN);
       const uint32_t empty_off = smem_u32(empty), accf_off = smem_u32(acc_full);
-      uint32_t stage = 0, phase = 0, acc_phase = 0;
+      uint32_t stage = 0, phase = 0, acc_phase = 0, region = 0;
       bool ok = true;
       for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
         if (!mbar_wait(acc_empty, acc_phase ^ 1u, p.status, kStatusTimeoutAccEmpty, abort_flag)) {
@@ -240,32 +256,38 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           break;
         }
         tc_fence_after();
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+        for (int kt = 0; kt < k_iters; ++kt) {
           if (!mbar_wait(&ready[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
+          const int nkb = min(kPairKBlocks, p.sf_kblocks - kPairKBlocks * kt);
           const uint64_t da = sdesc_kmajor_sw128(smem_u32(smem + kPairOffA + stage * kPairABytes));
           const uint64_t db = sdesc_kmajor_sw128(smem_u32(smem + kPairOffB + stage * kPairBBytes));
-          const uint32_t tsfa = tmem + kPairSfaCol + stage * kPairSfColsPerStage;
-          const uint32_t tsfb = tsfa + 4 * kKBlocksPerTile;
-          if (nkb == kKBlocksPerTile) {
+          const uint32_t tsfa = tmem + kPairSfaCol + region * kPairSfColsPerStage;
+          const uint32_t tsfb = tsfa + 4 * kPairKBlocks;
+          // block j: swizzle atom j / 4 (kPairAtomBytes apart), 32-byte K step j % 4 inside it
+          if (nkb == kPairKBlocks) {
 #pragma unroll
-            for (int j = 0; j < kKBlocksPerTile; ++j)
-              tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
+            for (int j = 0; j < kPairKBlocks; ++j) {
+              const uint32_t off = (j >> 2) * (kPairAtomBytes >> 4) + 2 * (j & 3);
+              tc_mma_nvf4_pair(tmem + kAccCol, da + off, db + off, idesc, tsfa + 4 * j, tsfb + 8 * j,
                                (kt | j) != 0 ? 1u : 0u);
+            }
           } else {
-            for (int j = 0; j < nkb; ++j)
-              tc_mma_nvf4_pair(tmem + kAccCol, da + 2 * j, db + 2 * j, idesc, tsfa + 4 * j, tsfb + 8 * j,
+            for (int j = 0; j < nkb; ++j) {
+              const uint32_t off = (j >> 2) * (kPairAtomBytes >> 4) + 2 * (j & 3);
+              tc_mma_nvf4_pair(tmem + kAccCol, da + off, db + off, idesc, tsfa + 4 * j, tsfb + 8 * j,
                                (kt | j) != 0 ? 1u : 0u);
+            }
           }
           tc_commit_pair_mc(empty_off + 8u * stage, 0x3);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1u;
           }
+          if (++region == kPairSfRegions) region = 0;
         }
         if (!ok) break;
         tc_commit_pair_mc(accf_off, 0x3);
@@ -280,42 +302,55 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   } else if (warp == 3 || warp == 4 || warp == 9) {
     // ------------------------------------------------------------------ scale copies (CTA 0)
     // Warp 3 copies the A scales (one 512-byte chunk per 64-element block), warps 4 and 9 the B
-    // scales of tile rows 0-127 and 128-255. K-tile g lands in scale slot g % 8 and
-    // is copied into the TMEM region of A/B stage g % 5 once the MMAs of k-tile g - 5, the last
-    // readers of that region, have completed.
+    // scales of tile rows 0-127 and 128-255. Stage iteration g lands in scale slot g % Q and is
+    // copied into TMEM region g % R once the MMAs of iteration g - R, the last readers of that
+    // region, have completed: completion number (g - R) / S of the empty barrier of A/B stage
+    // (g - R) % S. That barrier cannot run two completions ahead, since iteration g + 1 needs
+    // these copies first.
     if (leader && lane == 0) {
       const bool is_a = warp == 3;
       const int half = warp == 9 ? 1 : 0;  // B-scale copy warps: which 128 rows of the tile
       const int role = is_a ? 1 : 2 + half;  // drain barrier index
       const uint32_t sfe_off = smem_u32(sf_empty);
-      uint32_t stage = 0, phase = 0, slot = 0, sphase = 0;
+      uint32_t stage = 0, phase = 0, slot = 0, sphase = 0, region = 0;
+      uint32_t lag_stage = 0, lag_phase = 0;  // A/B stage and completion parity of iteration g - R
+      int it = 0;
       bool ok = true;
       for (int t = pair; ok && t < p.num_tiles; t += num_pairs) {
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!mbar_wait(&sf_full[slot], sphase, p.status, kStatusTimeoutFull, abort_flag) ||
-              !mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutEmpty, abort_flag)) {
+        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+          if (!mbar_wait(&sf_full[slot], sphase, p.status, kStatusTimeoutFull, abort_flag)) {
             ok = false;
             break;
           }
+          if (it >= kPairSfRegions) {
+            if (!mbar_wait(&empty[lag_stage], lag_phase, p.status, kStatusTimeoutEmpty, abort_flag)) {
+              ok = false;
+              break;
+            }
+            if (++lag_stage == kPairStages) {
+              lag_stage = 0;
+              lag_phase ^= 1u;
+            }
+          }
           tc_fence_after();
-          const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
-          const uint32_t tsfa = tmem + kPairSfaCol + stage * kPairSfColsPerStage;
-          const uint32_t tsfb = tsfa + 4 * kKBlocksPerTile;
+          const int nkb = min(kPairKBlocks, p.sf_kblocks - kPairKBlocks * kt);
+          const uint32_t tsfa = tmem + kPairSfaCol + region * kPairSfColsPerStage;
+          const uint32_t tsfb = tsfa + 4 * kPairKBlocks;
           if (is_a) {
             const uint64_t dsa = sdesc_sf_chunk(smem_u32(smem + kPairOffSfa + slot * kPairSfaBytes));
-            if (nkb == kKBlocksPerTile) {
+            if (nkb == kPairKBlocks) {
 #pragma unroll
-              for (int j = 0; j < kKBlocksPerTile; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
+              for (int j = 0; j < kPairKBlocks; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
             } else {
               for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4_pair(tsfa + 4 * j, dsa + 32 * j);
             }
           } else {
             const uint64_t dsb =
-                sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + slot * kPairSfbBytes)) + 32 * kKBlocksPerTile * half;
+                sdesc_sf_chunk(smem_u32(smem + kPairOffSfb + slot * kPairSfbBytes)) + 32 * kPairKBlocks * half;
             const uint32_t tb = tsfb + 4 * half;
-            if (nkb == kKBlocksPerTile) {
+            if (nkb == kPairKBlocks) {
 #pragma unroll
-              for (int j = 0; j < kKBlocksPerTile; ++j) tc_cp_32x128b_warpx4_pair(tb + 8 * j, dsb + 32 * j);
+              for (int j = 0; j < kPairKBlocks; ++j) tc_cp_32x128b_warpx4_pair(tb + 8 * j, dsb + 32 * j);
             } else {
               for (int j = 0; j < nkb; ++j) tc_cp_32x128b_warpx4_pair(tb + 8 * j, dsb + 32 * j);
             }
@@ -323,7 +358,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           // The TMEM region goes to the MMA thread as soon as the copies are issued: the fence
           // orders them before this arrive, the MMA thread's after_thread_sync fence orders its
           // MMAs after it, and the tensor pipe runs them in that order. Warp 3 also waits for the
-          // stage's A/B data, so the MMA thread waits on one barrier per k-tile. The
+          // stage's A/B data, so the MMA thread waits on one barrier per stage. The
           // shared-memory slot is freed only when the copies have completed.
           tc_fence_before();
           if (is_a && !mbar_wait(&full[stage], phase, p.status, kStatusTimeoutFull, abort_flag)) {
@@ -340,6 +375,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             slot = 0;
             sphase ^= 1u;
           }
+          if (++region == kPairSfRegions) region = 0;
         }
       }
       if (!ok) {
