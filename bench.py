@@ -266,15 +266,21 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------- GPU path
-def make_operands(rows, k, seed, dev):
-    """Seeded N(0,1) BF16 -> NVFP4 with the on-device global scale."""
+def make_operands(rows, k, seed, dev, sharded=False):
+    """Seeded N(0,1) BF16 -> NVFP4 with the on-device global scale. `sharded`: these rows are
+    this rank's block of a tensor split over the process group, quantised with the whole
+    tensor's global scale (one all-reduce of the amax)."""
     import torch
 
     import gemm3_b200 as g3
+    from gemm3_b200 import dist as g3dist
 
     g = torch.Generator(device=dev).manual_seed(seed)
     x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
-    q, sf, _, gs = g3.quantize_nvfp4_global(x)
+    if sharded:
+        q, sf, _, gs = g3dist.quantize_shard_global(x)
+    else:
+        q, sf, _, gs = g3.quantize_nvfp4_global(x)
     del x
     return q, sf, gs
 
@@ -307,7 +313,8 @@ def run_ours(args):
     sets = []
     for s in range(n_sets):
         a_q, a_sf, gs_a = make_operands(M, K, seed=1000 * s, dev=dev)  # A replicated: same seed on every rank
-        b_q, b_sf, gs_b = make_operands(N, K, seed=1000 * s + 1 + 7919 * rank, dev=dev)  # this rank's B block
+        # this rank's block of B (N rows of the N * world), with B's global scale over all ranks
+        b_q, b_sf, gs_b = make_operands(N, K, seed=1000 * s + 1 + 7919 * rank, dev=dev, sharded=world > 1)
         alpha = (1.0 / (gs_a * gs_b)).reshape(1).float()
         sets.append((a_q, b_q, a_sf, b_sf, alpha))
     c = torch.empty(M, N, dtype=out_dtype, device=dev)
@@ -432,26 +439,37 @@ def run_ours(args):
 
 
 def time_allgather(c, world, dev):
+    """The optional gather of the C blocks over NVLink (NCCL all-gather into [world * M, N_local])
+    and, separately, its relayout into row-major [M, N]; device time, max over ranks."""
     import torch
     import torch.distributed as dist
 
-    out = torch.empty((world,) + tuple(c.shape), dtype=c.dtype, device=dev)
+    from gemm3_b200 import dist as g3dist
+
+    m, n_local = c.shape
+    gathered = torch.empty((world * m, n_local), dtype=c.dtype, device=dev)
+    full = torch.empty((m, world * n_local), dtype=c.dtype, device=dev)
     for _ in range(3):
-        dist.all_gather_into_tensor(out, c)
+        g3dist.all_gather_columns(c, out=full, gathered=gathered)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 10
-    e0.record()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
     for _ in range(reps):
-        dist.all_gather_into_tensor(out, c)
-    e1.record()
+        dist.all_gather_into_tensor(gathered, c)
+    ev[1].record()
+    for _ in range(reps):
+        full.view(m, world, n_local).copy_(gathered.view(world, m, n_local).permute(1, 0, 2))
+    ev[2].record()
     torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+    ms = torch.tensor([ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps], dtype=torch.float64,
+                      device=dev)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = ms.item()
+    gather_ms, relayout_ms = ms.tolist()
     nbytes = c.numel() * c.element_size() * world
-    return {"ms": ms, "bytes_gathered": nbytes, "bus_gbs": nbytes * (world - 1) / world / (ms * 1e-3) / 1e9,
-            "layout": "[world][M][N/world] (NCCL order)"}
+    return {"ms": gather_ms, "relayout_ms": relayout_ms, "bytes_gathered": nbytes,
+            "bus_gbs": nbytes * (world - 1) / world / (gather_ms * 1e-3) / 1e9,
+            "layout": "NCCL all-gather to [world*M][N/world], then one copy to row-major [M][N]"}
 
 
 def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):
