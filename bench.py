@@ -51,6 +51,11 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-rows", type=int, default=128)
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--llm", action="store_true",
+                   help="BASELINE config 4: N=28672, K=8192 weight against M in --llm-m activations, "
+                        "activation quantisation + GEMM per call; one JSON line per M")
+    p.add_argument("--llm-m", default="16,128,1024,8192")
+    p.add_argument("--llm-tile", default="auto", choices=["auto", "256", "128"])
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     return args
@@ -521,10 +526,100 @@ def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):
     }
 
 
+def run_llm(args):
+    """BASELINE config 4 on one GPU: y = x . W^T with W [28672, 8192] ~ N(0, 0.02) (quantised once,
+    global scale) and x [M, 8192] ~ N(0, 1) with 1% of the columns (82, seeded) scaled by 20. Each
+    call quantises x on the GPU (amax, then codes and scales with gs = 2688 / amax), forms
+    alpha = 1 / (gs_x * gs_W) on the device and runs the GEMM; the call is one CUDA graph. Several
+    copies of W larger than L2 in total rotate between calls, so W streams from HBM."""
+    import torch
+
+    import gemm3_b200 as g3
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    assert g3.supported(), "needs sm_100 and the built extension"
+    N, K = 28672, 8192
+    _, _, l2 = g3.hw.device_info(0)
+    w_bytes = N * K // 2 + N * K // 16
+    n_w = max(2, math.ceil(3 * l2 / w_bytes))
+    gw = torch.Generator(device=dev).manual_seed(3)
+    weights = []
+    for _ in range(n_w):
+        w = (torch.randn(N, K, device=dev, generator=gw) * 0.02).to(torch.bfloat16)
+        wq, wsf, _, gs_w = g3.quantize_nvfp4_global(w)
+        weights.append((wq, wsf, gs_w))
+        del w
+    bf16_peak, hbm_peak, _ = peaks()
+    lines = []
+    for m in [int(x) for x in args.llm_m.split(",")]:
+        gx = torch.Generator(device=dev).manual_seed(4)
+        x = torch.randn(m, K, device=dev, generator=gx)
+        cols = torch.randperm(K, generator=torch.Generator().manual_seed(5))[: K // 100].to(dev)
+        x[:, cols] *= 20.0
+        x = x.to(torch.bfloat16)
+        out = torch.empty(m, N, dtype=torch.bfloat16, device=dev)
+        tile = (256, 256) if args.llm_tile == "256" else (128, 256) if args.llm_tile == "128" else None
+        cfg = g3.config_for(m, N, K) if tile is None else g3.Config.make(tile=tile)
+
+        def call(i):
+            wq, wsf, gs_w = weights[i % n_w]
+            xq, xsf, _, gs_x = g3.quantize_nvfp4_global(x)
+            alpha = torch.reciprocal(gs_x * gs_w)
+            g3.gemm(xq, wq, xsf, wsf, alpha=alpha, out=out, out_dtype=torch.bfloat16, config=cfg)
+
+        for i in range(n_w):
+            call(i)
+        torch.cuda.synchronize()
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        graphs = []
+        with torch.cuda.stream(stream):
+            for i in range(n_w):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    call(i)
+                graphs.append(gr)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        for i in range(max(args.warmup, 3)):
+            graphs[i % n_w].replay()
+        torch.cuda.synchronize()
+        steps = max(args.steps // 10, 50)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            graphs[i % n_w].replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / steps * 1e3
+        status = g3.device_status()
+        if status:
+            raise RuntimeError(f"device status {status}")
+        flops = 2.0 * m * N * K
+        wbytes = w_bytes + m * K * 2 + m * K // 2 + 2 * m * N  # W once, x read + codes, y written
+        line = {
+            "metric": "NVFP4 LLM-projection call (activation quantise + GEMM), us per call",
+            "value": us, "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": steps,
+            "config": {"workload": f"x[{m},{K}] . W[{N},{K}]^T, BF16 out, activation quantised per call",
+                       "tile": list(cfg.tile), "l2": f"cold: {n_w} rotating weight copies"},
+            "tflops": flops / (us * 1e-6) / 1e12,
+            "hbm_gbs": wbytes / (us * 1e-6) / 1e9,
+            "hbm_frac": wbytes / (us * 1e-6) / 1e9 / hbm_peak if hbm_peak else None,
+            "fp4_frac": flops / (us * 1e-6) / 1e12 / (4.0 * bf16_peak),
+            "data": "synthetic: W ~ N(0, 0.02), x ~ N(0, 1) with 1% of columns x20",
+        }
+        lines.append(line)
+        print(json.dumps(line), flush=True)
+        del graphs
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.llm:
+        return run_llm(args)
     return run_ours(args)
 
 

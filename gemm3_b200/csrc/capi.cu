@@ -278,7 +278,10 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   if (rc != NVFP4_OK) return rc;
 
   CUtensorMap tmap_a, tmap_b, tmap_sfa, tmap_sfb;
-  rc = encode_operand(&tmap_a, a, m, k / 2, g3::kTileM);
+  // A box rows: 128, or for the one-CTA kernel with M < 128 just the rows that exist (rounded
+  // up to 8, the swizzle atom).
+  const int64_t a_box_rows = (!pair && m < g3::kTileM) ? (m + 7) / 8 * 8 : g3::kTileM;
+  rc = encode_operand(&tmap_a, a, m, k / 2, static_cast<uint32_t>(a_box_rows));
   if (rc != NVFP4_OK) return rc;
   rc = encode_operand(&tmap_b, b, n, k / 2, pair ? 128 : g3::kTileN);
   if (rc != NVFP4_OK) return rc;
@@ -303,6 +306,7 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   p.n_tiles = static_cast<int>((n + g3::kTileN - 1) / g3::kTileN);
   p.k_tiles = static_cast<int>((k + 255) / 256);
   p.sf_kblocks = static_cast<int>(k / 64);
+  p.a_box_bytes = static_cast<int>(a_box_rows) * g3::kTileKBytes;
   p.n_rowblocks = static_cast<int>((n + 127) / 128);
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
   if (tiles > INT32_MAX) return NVFP4_ERR_INVALID_VALUE;

@@ -71,6 +71,11 @@ struct GemmParams {
   int store_evict_first;
   int pace_ns;
   int tma_b_first;
+  // Bytes of one A box of the one-CTA kernel: 128 B x min(128, M rounded up to 8) rows. With
+  // fewer than 128 rows of A the box covers only the rows that exist: rows of shared memory
+  // beyond it hold stale data, which feeds only output rows >= M, and those are not stored.
+  // (A 128-row box over an operand of under 32 rows runs at about half speed on B200.)
+  int a_box_bytes;
 };
 
 // Linear persistent work index -> (m-tile, n-tile). Bands of `raster_band` tiles along one
@@ -166,7 +171,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           const int nkb = min(kKBlocksPerTile, p.sf_kblocks - kKBlocksPerTile * kt);
           const uint32_t sf_bytes = static_cast<uint32_t>(nkb * kSfChunk);
-          mbar_arrive_expect_tx(&full[stage], kABytes + kBBytes + sf_bytes * (1 + nrb));
+          mbar_arrive_expect_tx(&full[stage], p.a_box_bytes + kBBytes + sf_bytes * (1 + nrb));
           uint8_t* sa = smem + kOffA + stage * kABytes;
           uint8_t* sb = smem + kOffB + stage * kBBytes;
           if (p.tma_b_first) {

@@ -30,7 +30,9 @@ def test_config_make_and_presets():
     assert c.tile == (256, 256) and c.cluster == (8, 2) and c.fallback == (2, 1)
     assert c.attrs == (("fast_swz", 4), ("l2_policy_a", "evict_last"))
     assert Config.make(fallback=None).fallback is None
-    assert config_for(1, 2, 3) == g3.DEFAULT
+    assert config_for(1024, 2048, 4096) == g3.DEFAULT
+    assert config_for(16, 28672, 8192).tile == (128, 256)  # B200 skinny retune for M <= 128
+    assert config_for(129, 28672, 8192) == g3.DEFAULT
     for size in (4096, 8192, 16384, 32768):
         assert config_for(size, size, size) is g3.PRESETS[(size, size, size)]
 

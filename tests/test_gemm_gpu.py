@@ -82,10 +82,12 @@ def test_accuracy_contract_fp64(cuda_ext, dtype):
 
 @pytest.mark.parametrize(
     "m,n,k",
-    [(1, 64, 64), (129, 64, 128), (128, 320, 320), (300, 192, 1088), (77, 576, 64), (256, 256, 2304)],
+    [(1, 64, 64), (129, 64, 128), (128, 320, 320), (300, 192, 1088), (77, 576, 64), (256, 256, 2304),
+     (8, 512, 1024), (16, 1024, 2048), (24, 768, 512)],
 )
 def test_edge_shapes_vs_oracle(cuda_ext, m, n, k):
-    """Ragged M, N not a multiple of the 256-column tile, K tails of 1-3 scale blocks."""
+    """Ragged M, N not a multiple of the 256-column tile, K tails of 1-3 scale blocks, and skinny M
+    (fewer than 32 rows: the A box covers only the rows present)."""
     inp = _inputs(cuda_ext, m, n, k, seed=m + n + k)
     out = cuda_ext.gemm(inp["a"], inp["b"], inp["a_sf"], inp["b_sf"])
     c64 = oracle.gemm_fp64(*(inp[x].cpu().numpy() for x in ("a", "a_sf_linear", "b", "b_sf_linear")))
