@@ -47,6 +47,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--allgather", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-vendor", action="store_true", help="skip the cuBLASLt timing on the same workload")
     p.add_argument("--e2e-steps", type=int, default=12)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-rows", type=int, default=128)
@@ -388,6 +389,10 @@ def run_ours(args):
     if args.allgather and world > 1:
         allgather = time_allgather(c, world, dev)
 
+    vendor = None
+    if world == 1 and not args.no_vendor:
+        vendor = time_cublaslt(sets, out_dtype, dev, M, N, K)
+
     e2e = None
     if not args.no_e2e:
         e2e = time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world)
@@ -432,6 +437,7 @@ def run_ours(args):
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "vendor": vendor,
     }
     if allgather is not None:
         line["allgather"] = allgather
@@ -475,6 +481,52 @@ def time_allgather(c, world, dev):
     return {"ms": gather_ms, "relayout_ms": relayout_ms, "bytes_gathered": nbytes,
             "bus_gbs": nbytes * (world - 1) / world / (gather_ms * 1e-3) / 1e9,
             "layout": "NCCL all-gather to [world*M][N/world], then one copy to row-major [M][N]"}
+
+
+def time_cublaslt(sets, out_dtype, dev, M, N, K):
+    """cuBLASLt's NVFP4 GEMM on the same rotating inputs (CUDA-graph replays, CUDA events): the
+    vendor baseline on this B200. Outputs are bit-identical to gemm3_b200.gemm (tests/)."""
+    import torch
+
+    try:
+        from gemm3_b200.cublaslt import gemm_cublaslt
+    except Exception as exc:  # adapter not built on this toolkit
+        return {"unavailable": str(exc)}
+    c = torch.empty(M, N, dtype=out_dtype, device=dev)
+    alphas = [float(s[4].item()) for s in sets]
+
+    def step(i):
+        a_q, b_q, a_sf, b_sf, _ = sets[i % len(sets)]
+        gemm_cublaslt(a_q, b_q, a_sf, b_sf, alpha=alphas[i % len(sets)], out=c, out_dtype=out_dtype)
+
+    for i in range(len(sets)):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    graphs = []
+    with torch.cuda.stream(stream):
+        for i in range(len(sets)):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step(i)
+            graphs.append(gr)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    for i in range(10):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    lat = []
+    for i in range(64):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graphs[i % len(graphs)].replay()
+        e1.record()
+        lat.append((e0, e1))
+    torch.cuda.synchronize()
+    us = statistics.median(a.elapsed_time(b) for a, b in lat) * 1e3
+    del graphs
+    return {"impl": "cuBLASLt (same GPU, same inputs, outputs bit-identical)", "us_per_gemm": us,
+            "pflops": 2.0 * M * N * K / (us * 1e-6) / 1e15}
 
 
 def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):

@@ -42,19 +42,27 @@ def nvcc_path():
     raise RuntimeError("nvcc not found; the CUDA toolkit is required to build gemm3_b200")
 
 
-def up_to_date():
-    if not os.path.exists(LIB_PATH):
+# The cuBLASLt adapter (vendor baseline, not on the compute path): a separate library that links
+# the toolkit's libcublasLt, found at run time through this rpath or an already loaded copy.
+CUBLASLT_LIB_PATH = os.path.join(PKG_DIR, "libgemm3_b200_cublaslt.so")
+CUBLASLT_SOURCES = [os.path.join(CSRC, "cublaslt_adapter.cu")]
+CUBLASLT_DEPENDS = CUBLASLT_SOURCES + [os.path.join(REPO_DIR, "include", "nvfp4_cublaslt.h")]
+
+
+def _cuda_root():
+    return os.path.dirname(os.path.dirname(os.path.realpath(nvcc_path())))
+
+
+def up_to_date(path=LIB_PATH, depends=DEPENDS):
+    if not os.path.exists(path):
         return False
-    t = os.path.getmtime(LIB_PATH)
-    return all(os.path.getmtime(f) <= t for f in DEPENDS)
+    t = os.path.getmtime(path)
+    return all(os.path.getmtime(f) <= t for f in depends)
 
 
-def build(force=False, verbose=False):
-    """Compile the extension unless it is newer than every source. Returns the library path."""
-    if not force and up_to_date():
-        return LIB_PATH
-    tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
+def _compile(path, sources, extra, verbose):
+    tmp = path + ".tmp"
+    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *sources, *extra]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
@@ -62,7 +70,27 @@ def build(force=False, verbose=False):
     if res.returncode != 0:
         msg = (res.stderr or "") + (res.stdout or "")
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{msg}")
-    os.replace(tmp, LIB_PATH)
+    os.replace(tmp, path)
+
+
+def build_cublaslt(force=False, verbose=False):
+    """Compile the cuBLASLt adapter if the toolkit has cuBLASLt. Returns its path, or None."""
+    root = _cuda_root()
+    lib_dir = os.path.join(root, "lib64")
+    if not os.path.exists(os.path.join(root, "include", "cublasLt.h")):
+        return None
+    if force or not up_to_date(CUBLASLT_LIB_PATH, CUBLASLT_DEPENDS):
+        _compile(CUBLASLT_LIB_PATH, CUBLASLT_SOURCES, [f"-L{lib_dir}", "-lcublasLt", f"-Xlinker=-rpath,{lib_dir}"],
+                 verbose)
+    return CUBLASLT_LIB_PATH
+
+
+def build(force=False, verbose=False):
+    """Compile the extension (and the cuBLASLt adapter) unless newer than every source. Returns
+    the extension's path."""
+    if force or not up_to_date():
+        _compile(LIB_PATH, SOURCES, [], verbose)
+    build_cublaslt(force, verbose)
     return LIB_PATH
 
 

@@ -69,3 +69,20 @@ def test_argument_validation_without_gpu(L):
 
 def test_config_struct_layout():
     assert ctypes.sizeof(_lib.GemmConfig) == 13 * 4
+
+
+def test_cublaslt_adapter_exports_its_header():
+    from gemm3_b200 import cublaslt
+
+    path = build.build_cublaslt()
+    assert path is not None, "the toolkit has cuBLASLt; the adapter must build"
+    hdr = os.path.join(os.path.dirname(HEADER), "nvfp4_cublaslt.h")
+    text = re.sub(r"/\*.*?\*/", "", open(hdr).read(), flags=re.S)
+    declared = set(re.findall(r"\b(nvfp4_[a-z0-9_]+)\s*\(", text))
+    assert declared == set(cublaslt.EXPORTED_SYMBOLS)
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True)
+    assert declared <= set(re.findall(r"\bT (nvfp4_\w+)", out.stdout))
+    L = cublaslt.lib()
+    p = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
+    assert L.nvfp4_cublaslt_gemm(p, p, p, p, p, 1.0, 128, 100, 128, 0, None, 0, None) == 1  # N % 64
+
