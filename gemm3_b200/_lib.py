@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_last_cuda_error",
     "nvfp4_abi_version",
     "nvfp4_quantize_global_noalloc",
+    "nvfp4_selftest_wait_timeout",
 )
 
 
@@ -85,6 +86,7 @@ _SIGNATURES = {
     "nvfp4_last_cuda_error": (_i32, []),
     "nvfp4_abi_version": (_i32, []),
     "nvfp4_quantize_global_noalloc": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "nvfp4_selftest_wait_timeout": (ctypes.c_int, [_vp, _i32, _vp]),
 }
 
 

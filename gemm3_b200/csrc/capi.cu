@@ -169,11 +169,31 @@ int quant_grid(DeviceCache* d, int32_t in_dtype, int64_t work) {
   return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
+// A bounded wait that can never complete: one thread waits on a fresh mbarrier (count 1) that
+// nothing arrives at, through the same mbar_wait the GEMM kernels use. After kWaitTimeoutNs it
+// records `code` in *status and returns; the kernel then exits normally.
+__global__ void wait_timeout_selftest_kernel(int* status, int code) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    g3::mbar_init(&bar, 1);
+    g3::fence_mbarrier_init();
+    if (g3::mbar_wait(&bar, 0, status, code, nullptr)) atomicExch(status, -1);  // cannot happen
+  }
+}
+
 }  // namespace
 
 extern "C" {
 
 int32_t nvfp4_abi_version(void) { return 1; }
+
+int nvfp4_selftest_wait_timeout(int32_t* status, int32_t code, void* stream) {
+  if (status == nullptr || code < NVFP4_DEV_TIMEOUT_FULL || code > NVFP4_DEV_ABORTED) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(status, 4)) return NVFP4_ERR_MISALIGNED;
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<int*>(status), code);
+  G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
 
 int32_t nvfp4_last_cuda_error(void) { return g_last_cuda_error; }
 

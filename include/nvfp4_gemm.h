@@ -162,6 +162,15 @@ int nvfp4_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major, int3
  * (nvfp4_gemm_cute/api.py:223-242). A per-context limit: it ends with the process. */
 int nvfp4_set_persisting_l2(int64_t bytes, int64_t* old_bytes);
 
+/*
+ * Failure-detection self-test; no counterpart in the reference. Launches one thread that waits,
+ * through the bounded wait every GEMM kernel uses, on an mbarrier that nothing arrives at. After
+ * the wait limit (2 s) it writes `code` (one of NVFP4_DEV_*) to the device int32 *status, if
+ * *status is still 0, and the kernel exits; the context stays usable. Lets a test check that a
+ * wait which cannot complete ends with a status instead of a hang.
+ */
+int nvfp4_selftest_wait_timeout(int32_t* status, int32_t code, void* stream);
+
 /* Human-readable text for a status code; static storage. */
 const char* nvfp4_strerror(int32_t code);
 
