@@ -22,8 +22,9 @@
 // magnitude code is 0 however q rounds, and the sign bit is decided from xb and the scale
 // directly (e2m1_pack16).
 //
-// Per element the work is FP32 multiply-adds only (the threshold tests are saturating FMAs), so
-// the kernel is not limited by the integer/compare pipe, which has half the FMA pipe's rate.
+// The codes themselves come from the hardware E2M1 conversion (round-to-nearest-even); the
+// reference's tie rule is applied exactly by a check that sends only elements next to a rounding
+// tie to its thresholds (e2m1_pack8).
 //
 // One thread owns one 16-element scale block. Consecutive threads own consecutive blocks of
 // the row-major input, so loads (32 or 64 bytes per thread), code stores (8 bytes) and linear
@@ -68,57 +69,83 @@ __device__ __constant__ float kE2M1Table[9] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0
 constexpr uint32_t kE2M1T1 = 0x3E800012u, kE2M1T2 = 0x3F3FFFF8u, kE2M1T3 = 0x3FA00005u, kE2M1T4 = 0x3FDFFFFCu,
                    kE2M1T5 = 0x40200003u, kE2M1T6 = 0x405FFFFEu, kE2M1T7 = 0x40A00002u;
 
-// d = sat(a * b + c) and d = sat(a * b), one rounding each; sat clamps to [0, 1] (NaN -> 0).
+// d = sat(a * b + c), one rounding; sat clamps to [0, 1] (NaN -> 0).
 __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   float d;
   asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-__device__ __forceinline__ float mul_sat(float a, float b) {
-  float d;
-  asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
-  return d;
+
+// E2M1 magnitude code (0-7) of |q| = mag by the reference's thresholds, exactly: with P = the
+// float below threshold T, the step sat(|q| * 2^100 - P * 2^100) is exactly 1 when |q| >= T (the
+// difference is at least one ulp, 2^-25, so the product is >= 2^75) and exactly 0 otherwise; the
+// code is the sum of the seven steps, accumulated on 2^23 so the float's low bits hold it.
+__device__ __forceinline__ uint32_t e2m1_mag_code_steps(float mag) {
+  float acc = 8388608.0f;
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.000022p+98f));  // T1 0x3E800012
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.7fffeep+99f));  // T2 0x3F3FFFF8
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400008p+100f)); // T3 0x3FA00005
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffff6p+100f)); // T4 0x3FDFFFFC
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400004p+101f)); // T5 0x40200003
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffffap+101f)); // T6 0x405FFFFE
+  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400002p+102f)); // T7 0x40A00002
+  return __float_as_uint(acc) - 0x4B000000u;
 }
 
-// Packed E2M1 codes of the sixteen quotients xb[i] / d (d > 0 finite, r = the correctly rounded
-// 1 / d): nibble i of the 64-bit result, sign in bit 3. All arithmetic is exact FP32 on the FMA
-// pipe, so the integer/compare pipe stays free:
-//  - magnitude: with P = the float below T, the step sat(|q| * 2^100 - P * 2^100) is exactly 1
-//    when |q| >= T (the difference is at least one ulp, 2^-25, so the product is >= 2^75) and
-//    exactly 0 otherwise; the code is the sum of the seven steps;
+// Hardware round-to-nearest-even of eight magnitudes to E2M1 (saturating at 6), packed two per
+// byte with element 2i in the low nibble: four cvt.e2m1x2 into one word.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(const float (&m)[8]) {
+  uint32_t w;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(w)
+      : "f"(m[0]), "f"(m[1]), "f"(m[2]), "f"(m[3]), "f"(m[4]), "f"(m[5]), "f"(m[6]), "f"(m[7]));
+  return w;
+}
+
+// Packed E2M1 codes (sign in bit 3, element 2i in the low nibble) of the eight quotients
+// xb[i] / d, given r = the correctly rounded 1 / d and d_lo = d * 2^-50.
+//  - magnitude: the reference's code equals round-to-nearest-even on the E2M1 grid except for
+//    |q| within a few ulps of one of the seven rounding ties, where its 1e-6 bias on odd codes
+//    moves the boundary (within 18 ulps, relative 2.2e-6). The hardware conversions of
+//    |q| * (1 - 2^-17) and |q| * (1 + 2^-17) agree exactly when no tie lies in between, and
+//    then that code is the reference's (checked on the CPU for every float in [0, 6.5]). An
+//    element whose two conversions differ takes the exact threshold steps instead.
 //  - sign: q = RN(xb / d) < 0 exactly when xb / d < -2^-150 (the tie at 2^-150 rounds to -0),
-//    i.e. when -xb * 2^100 - d * 2^-50 > 0; both products are exact and the FMA keeps the sign,
-//    and any positive result is a multiple of 2^-73, so multiplying by 2^127 and saturating
-//    gives exactly 1. Tiny xb therefore needs no division: its magnitude code is 0 whatever
-//    rounding the quotient sees, and its sign comes from xb and d directly;
-//  - the sum starts at 2^23, so the float's low mantissa bits are the code; the words are built
-//    with integer multiply-adds and the 2^23 bias (0x4B000000 per nibble) removed at the end.
-__device__ __forceinline__ uint2 e2m1_pack16(const float (&xb)[16], float d, float r) {
-  const float nd = -d;
-  const float d_lo = __fmul_rn(d, 0x1p-50f);
-  uint32_t w0 = 0, w1 = 0;
+//    i.e. when t = -xb * 2^100 - d * 2^-50 > 0; both products are exact and the FMA keeps the
+//    sign, so the bit is t's "greater than +0" test on its bit pattern (t is never -0: d > 0).
+//    Tiny xb therefore needs no division: its magnitude code is 0 whatever rounding the quotient
+//    sees, and its sign comes from xb and d directly.
+__device__ __forceinline__ uint32_t e2m1_pack8(const float* xb, float d, float r, float d_lo) {
+  float mag[8], lo[8], hi[8];
+  uint32_t neg = 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const float q1 = __fmul_rn(xb[i], r);
-    const float rem = __fmaf_rn(q1, nd, xb[i]);
-    const float mag = fabsf(__fmaf_rn(rem, r, q1));
-    const float neg = mul_sat(__fmaf_rn(-xb[i], 0x1p100f, -d_lo), 0x1p127f);
-    float acc = __fmaf_rn(neg, 8.0f, 8388608.0f);
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.000022p+98f));  // T1 0x3E800012
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.7fffeep+99f));  // T2 0x3F3FFFF8
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400008p+100f)); // T3 0x3FA00005
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffff6p+100f)); // T4 0x3FDFFFFC
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400004p+101f)); // T5 0x40200003
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffffap+101f)); // T6 0x405FFFFE
-    acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400002p+102f)); // T7 0x40A00002
-    const uint32_t bits = __float_as_uint(acc);  // 0x4B000000 + code
-    if (i < 8)
-      w0 += bits * (1u << (4 * i));
-    else
-      w1 += bits * (1u << (4 * (i - 8)));
+    const float rem = __fmaf_rn(q1, -d, xb[i]);
+    mag[i] = fabsf(__fmaf_rn(rem, r, q1));
+    lo[i] = __fmul_rn(mag[i], 0x1.ffffp-1f);   // 1 - 2^-17
+    hi[i] = __fmul_rn(mag[i], 0x1.00008p+0f);  // 1 + 2^-17
+    const float t = __fmaf_rn(-xb[i], 0x1p100f, -d_lo);
+    neg |= ((0u - __float_as_uint(t)) >> 31) << (4 * i + 3);
   }
-  // sum over nibbles of 0x4B000000 << 4i, modulo 2^32
-  return make_uint2(w0 - 0xFB000000u, w1 - 0xFB000000u);
+  uint32_t w = cvt_e2m1x8(lo);
+  const uint32_t near_tie = w ^ cvt_e2m1x8(hi);
+  if (near_tie != 0u) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((near_tie >> (4 * i)) & 0xFu) w = (w & ~(0xFu << (4 * i))) | (e2m1_mag_code_steps(mag[i]) << (4 * i));
+  }
+  return w | neg;
+}
+
+__device__ __forceinline__ uint2 e2m1_pack16(const float (&xb)[16], float d, float r) {
+  const float d_lo = __fmul_rn(d, 0x1p-50f);
+  return make_uint2(e2m1_pack8(xb, d, r, d_lo), e2m1_pack8(xb + 8, d, r, d_lo));
 }
 
 // Byte offset of scale (row, col) in the 128x4 swizzled layout with `c4` 4-column groups.
