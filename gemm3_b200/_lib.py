@@ -19,6 +19,7 @@ ERR_TENSOR_MAP = 5
 ERR_TOO_LARGE = 6
 
 NOALLOC_MAX_ELEMENTS = 1 << 31
+ACT_WORKSPACE_BYTES = 4096
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 L2_NORMAL, L2_EVICT_FIRST, L2_EVICT_LAST = 0, 1, 2
@@ -37,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "nvfp4_abi_version",
     "nvfp4_quantize_global_noalloc",
     "nvfp4_selftest_wait_timeout",
+    "nvfp4_quantize_act",
 )
 
 
@@ -57,6 +59,7 @@ class GemmConfig(ctypes.Structure):
         ("epi_store_pace_ns", ctypes.c_int32),
         ("tma_b_first", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
+        ("pdl", ctypes.c_int32),
     ]
 
 
@@ -87,6 +90,7 @@ _SIGNATURES = {
     "nvfp4_abi_version": (_i32, []),
     "nvfp4_quantize_global_noalloc": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "nvfp4_selftest_wait_timeout": (ctypes.c_int, [_vp, _i32, _vp]),
+    "nvfp4_quantize_act": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
 }
 
 

@@ -15,7 +15,7 @@ import torch
 
 from . import _lib
 from .hw import arch
-from .presets import config_for
+from .presets import STREAM_MAX_M, config_for
 
 _ALPHA_ONE = {}
 _STATUS = {}
@@ -133,20 +133,27 @@ def _check_shape_guards(m, n, k, cfg, attrs):
             raise ValueError(
                 f"packed_ab_desc requires tile=(256, 256), cluster={cluster}, fallback=(2, 1)"
             )
-    if cfg.tile not in ((256, 256), (128, 256)):
-        raise ValueError(f"unsupported tile {cfg.tile}; use (256, 256) or (128, 256)")
+    if cfg.tile not in ((256, 256), (128, 256), (128, 128)):
+        raise ValueError(f"unsupported tile {cfg.tile}; use (256, 256), (128, 256) or (128, 128)")
+    if cfg.tile == (128, 128) and m > STREAM_MAX_M:
+        raise ValueError(
+            f"tile (128, 128) streams B with all of A's rows in one tile and needs M <= {STREAM_MAX_M} "
+            f"(got M={m})"
+        )
 
 
-def _launch_config(m, k, cfg, attrs):
+def _launch_config(m, k, cfg, attrs, pdl=0):
     """Translate a Config + effective attributes into the C struct (cached)."""
-    key = (m, k, cfg.tile, cfg.cluster, tuple(sorted(attrs.items())))
+    key = (m, k, cfg.tile, cfg.cluster, tuple(sorted(attrs.items())), pdl)
     c = _CFG_CACHE.get(key)
     if c is not None:
         return c
     c = _lib.GemmConfig()
     c.struct_size = ctypes.sizeof(_lib.GemmConfig)
-    c.tile_m = 256 if cfg.tile[0] == 256 else 128  # 256: CTA-pair kernel, 128: one CTA per tile
-    c.tile_n = 256
+    # 256: CTA-pair kernel; 128: one CTA per 128x256 tile; (128, 128): weight-streaming kernel
+    c.tile_m = 256 if cfg.tile[0] == 256 else 128
+    c.tile_n = cfg.tile[1]
+    c.pdl = pdl if cfg.tile == (128, 128) else 0
     m_tiles = -(-m // 128)
     s = int(attrs.get("fast_swz", 1) or 1)
     if s > 1:
@@ -201,11 +208,20 @@ def gemm(
         alpha: optional float32 tensor with one element; defaults to 1.0.
         out: optional [M, N] output of out_dtype.
         config: a presets.Config; defaults to presets.config_for(M, N, K).
-        enable_pdl: accepted for interface compatibility; launches are plain stream launches.
+        enable_pdl: launch the weight-streaming kernel (tile (128, 128), the M <= 128 preset) with
+            programmatic dependent launch: its set-up overlaps the tail of the preceding kernel
+            and every load waits for that kernel. The other kernels launch plainly.
 
     Requires N % 64 == 0 and K % 64 == 0. Shape, attribute and preset checks raise ValueError
     before any GPU work.
     """
+    return _gemm(a, b, a_sf, b_sf, alpha, out, out_dtype, config, 1 if enable_pdl else 0)
+
+
+def _gemm(a, b, a_sf, b_sf, alpha, out, out_dtype, config, pdl):
+    """gemm() with the C config's programmatic-dependent-launch mode (0, 1 or 2; see
+    include/nvfp4_gemm.h). Mode 2 (weights loaded before the dependency wait) is for callers that
+    know the preceding kernel does not write B, such as linear.nvfp4_linear."""
     m, kp = a.shape
     n = b.shape[0]
     k = kp * 2
@@ -217,7 +233,7 @@ def gemm(
     attrs = _effective_attrs(m, cfg)
     _check_shape_guards(m, n, k, cfg, attrs)
     code = _out_code(out_dtype)
-    ccfg = _launch_config(m, k, cfg, attrs)
+    ccfg = _launch_config(m, k, cfg, attrs, pdl)
 
     dev = a.device
     if dev.type != "cuda":

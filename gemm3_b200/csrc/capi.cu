@@ -11,6 +11,7 @@
 #include "../../include/nvfp4_gemm.h"
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
+#include "gemm_stream_kernel.cuh"
 #include "quant_kernel.cuh"
 
 namespace {
@@ -38,6 +39,7 @@ struct DeviceCache {
   int cc_major = 0, cc_minor = 0;
   int64_t l2_bytes = 0;
   bool gemm_attr_set = false;
+  bool stream_attr_set = false;
   int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
   int quant_blocks[3] = {0, 0, 0};  // co-resident 256-thread quantiser blocks per SM, per input dtype
 };
@@ -181,6 +183,75 @@ __global__ void wait_timeout_selftest_kernel(int* status, int code) {
   }
 }
 
+// Weight-streaming kernel (gemm_stream_kernel.cuh) for M <= 128: B in 128-row tiles over a
+// persistent grid of at most one CTA per SM, all of A in the MMA's N dimension.
+int launch_stream(const void* a, const void* b, const void* sfa, const void* sfb, void* c, const float* alpha,
+                  int64_t m, int64_t n, int64_t k, int32_t out_dtype, const nvfp4_gemm_config& def, int32_t* status,
+                  void* stream) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  if (d->cc_major != 10) return NVFP4_ERR_UNSUPPORTED;
+  rc = get_encoder();
+  if (rc != NVFP4_OK) return rc;
+  const int n_mma = static_cast<int>((m + 15) / 16 * 16);
+  const int a_box_rows = static_cast<int>((m + 7) / 8 * 8);
+  CUtensorMap tmap_a, tmap_b;
+  rc = encode_operand(&tmap_a, a, m, k / 2, static_cast<uint32_t>(a_box_rows));
+  if (rc != NVFP4_OK) return rc;
+  rc = encode_operand(&tmap_b, b, n, k / 2, g3::kStreamTileN);
+  if (rc != NVFP4_OK) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!d->stream_attr_set) {
+      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   g3::kStreamSmemLimit));
+      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   g3::kStreamSmemLimit));
+      d->stream_attr_set = true;
+    }
+  }
+  g3::StreamParams p;
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb = static_cast<const uint8_t*>(sfb);
+  p.c = c;
+  p.alpha = alpha;
+  p.status = status;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.n_mma = n_mma;
+  p.a_box_rows = a_box_rows;
+  p.sf_kblocks = static_cast<int>(k / 64);
+  p.k_iters = (p.sf_kblocks + g3::kStreamKBlocks - 1) / g3::kStreamKBlocks;
+  p.num_tiles = static_cast<int>((n + g3::kStreamTileN - 1) / g3::kStreamTileN);
+  p.stages = g3::stream_stages(n_mma);
+  p.stage_bytes = g3::stream_stage_bytes(n_mma);
+  p.pdl = def.pdl;
+  p.pol_b = def.l2_policy_b;
+  p.pol_sfb = def.l2_policy_sfb;
+  int ctas = d->sm_count;
+  if (def.max_ctas > 0 && def.max_ctas < ctas) ctas = def.max_ctas;
+  if (ctas > p.num_tiles) ctas = p.num_tiles;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(ctas, 1, 1);
+  lc.blockDim = dim3(g3::kStreamThreads, 1, 1);
+  lc.dynamicSmemBytes = g3::stream_smem_bytes(n_mma);
+  lc.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = &attr;
+  lc.numAttrs = def.pdl != 0 ? 1 : 0;
+  if (out_dtype == NVFP4_DTYPE_BF16)
+    G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<true>, tmap_a, tmap_b, p));
+  else
+    G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<false>, tmap_a, tmap_b, p));
+  return NVFP4_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -281,9 +352,20 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
       !aligned(alpha, 4))
     return NVFP4_ERR_MISALIGNED;
   nvfp4_gemm_config def = {};
-  if (cfg != nullptr && cfg->struct_size >= static_cast<int32_t>(sizeof(nvfp4_gemm_config))) def = *cfg;
-  if ((def.tile_m != 0 && def.tile_m != 128 && def.tile_m != 256) || (def.tile_n != 0 && def.tile_n != 256))
+  if (cfg != nullptr && cfg->struct_size > 0) {
+    // The first struct_size bytes: fields added after the caller's version keep their defaults.
+    const size_t nbytes = static_cast<size_t>(cfg->struct_size) < sizeof(def) ? static_cast<size_t>(cfg->struct_size)
+                                                                             : sizeof(def);
+    std::memcpy(&def, cfg, nbytes);
+  }
+  if ((def.tile_m != 0 && def.tile_m != 128 && def.tile_m != 256) ||
+      (def.tile_n != 0 && def.tile_n != 256 && def.tile_n != 128))
     return NVFP4_ERR_INVALID_VALUE;
+  if (def.pdl < 0 || def.pdl > 2) return NVFP4_ERR_INVALID_VALUE;
+  if (def.tile_n == 128) {
+    if (def.tile_m != 128 || m > g3::kStreamMaxM) return NVFP4_ERR_INVALID_VALUE;
+    return launch_stream(a, b, sfa, sfb, c, alpha, m, n, k, out_dtype, def, status, stream);
+  }
   const bool pair = def.tile_m != 128;
   if (def.raster_band < 0) return NVFP4_ERR_INVALID_VALUE;
 
@@ -442,6 +524,77 @@ int nvfp4_amax(const void* x, int32_t in_dtype, int64_t numel, float* amax_out, 
     default: g3::nvfp4_amax_kernel<2><<<grid, 256, 0, s>>>(x, numel, bits); break;
   }
   G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+int nvfp4_quantize_act(const void* x, int32_t in_dtype, int64_t rows, int64_t k, const float* gs_other,
+                       float* gs_out, float* alpha_out, void* packed, void* sf_swizzled, void* workspace,
+                       void* stream) {
+  if (!x || !packed || !sf_swizzled || !workspace) return NVFP4_ERR_INVALID_VALUE;
+  if (rows < 1 || k < 16 || k % 16) return NVFP4_ERR_INVALID_VALUE;
+  if (in_dtype < NVFP4_DTYPE_F16 || in_dtype > NVFP4_DTYPE_F32) return NVFP4_ERR_INVALID_VALUE;
+  if (alpha_out != nullptr && gs_other == nullptr) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned(x, 16) || !aligned(packed, 8) || !aligned(workspace, 4)) return NVFP4_ERR_MISALIGNED;
+  if (!aligned(gs_other, 4) || !aligned(gs_out, 4) || !aligned(alpha_out, 4)) return NVFP4_ERR_MISALIGNED;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NVFP4_OK) return rc;
+  DeviceCache* d = nullptr;
+  rc = device_cache(dev, &d);
+  if (rc != NVFP4_OK) return rc;
+  if (d->cc_major != 10) return NVFP4_ERR_UNSUPPORTED;
+  static_assert(g3::kActMaxParts * 4 <= NVFP4_ACT_WORKSPACE_BYTES, "act workspace");
+  g3::QuantParams p;
+  p.x = x;
+  p.rows = rows;
+  p.k = k;
+  p.cols = k / 16;
+  p.rows_pad = (rows + 127) / 128 * 128;
+  p.cols_pad = (p.cols + 3) / 4 * 4;
+  p.gs = 1.0f;
+  p.gs_dev = nullptr;
+  p.gs_mode = 2;
+  p.div_mode = 0;  // CUDA torch: multiply by fl(1/6)
+  p.packed = static_cast<uint8_t*>(packed);
+  p.sf_swz = static_cast<uint8_t*>(sf_swizzled);
+  p.sf_lin = nullptr;
+  p.gs_out = gs_out;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // amax: two 16-element vectors per thread, at most kActMaxParts CTAs
+  const int64_t nvec = rows * k / 16;
+  int64_t parts = (nvec + 2 * g3::kActThreads - 1) / (2 * g3::kActThreads);
+  const int64_t cap = static_cast<int64_t>(d->sm_count) * 4 < g3::kActMaxParts ? static_cast<int64_t>(d->sm_count) * 4
+                                                                                : g3::kActMaxParts;
+  if (parts > cap) parts = cap;
+  if (parts < 1) parts = 1;
+  uint32_t* ws = static_cast<uint32_t*>(workspace);
+  switch (in_dtype) {
+    case NVFP4_DTYPE_F16: g3::nvfp4_act_amax_kernel<0><<<static_cast<int>(parts), g3::kActThreads, 0, s>>>(x, rows * k, ws); break;
+    case NVFP4_DTYPE_BF16: g3::nvfp4_act_amax_kernel<1><<<static_cast<int>(parts), g3::kActThreads, 0, s>>>(x, rows * k, ws); break;
+    default: g3::nvfp4_act_amax_kernel<2><<<static_cast<int>(parts), g3::kActThreads, 0, s>>>(x, rows * k, ws); break;
+  }
+  G3_CUDA(cudaGetLastError());
+  // At most one quantiser CTA per SM: they become resident early (programmatic launch) and wait
+  // for the amax kernel, and each SM must keep room for a weight-streaming GEMM CTA (launched
+  // early the same way) beside it.
+  int qgrid = quant_grid(d, in_dtype, p.rows_pad * p.cols_pad);
+  if (qgrid > d->sm_count) qgrid = d->sm_count;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(qgrid), 1, 1);
+  lc.blockDim = dim3(g3::kActThreads, 1, 1);
+  lc.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = &attr;
+  lc.numAttrs = 1;
+  const uint32_t* cparts = ws;
+  const int nparts = static_cast<int>(parts);
+  switch (in_dtype) {
+    case NVFP4_DTYPE_F16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<0>, p, cparts, nparts, gs_other, alpha_out)); break;
+    case NVFP4_DTYPE_BF16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<1>, p, cparts, nparts, gs_other, alpha_out)); break;
+    default: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<2>, p, cparts, nparts, gs_other, alpha_out)); break;
+  }
   return NVFP4_OK;
 }
 

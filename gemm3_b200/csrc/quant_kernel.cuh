@@ -35,6 +35,8 @@
 
 #include <cstdint>
 
+#include "ptx.cuh"
+
 namespace g3 {
 
 // FP32 -> E4M3 (fn variant: bias 7, max 448, 0x7F/0xFF = NaN, no infinities), round to nearest
@@ -208,11 +210,39 @@ __device__ __forceinline__ float resolve_global_scale(const QuantParams& p) {
   return (v > 0.0f && v <= 3.402823466e38f) ? __fdiv_rn(2688.0f, v) : 1.0f;
 }
 
+// One 16-element block (r, c) of the padded scale grid: codes, linear and swizzled scale. Blocks
+// outside the logical shape write a zero scale into the swizzled padding only.
+template <int kInDtype>
+__device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, int64_t r, int64_t c, int64_t c4) {
+  const float inv6 = 0.166666672f;  // fl(1/6): what torch on CUDA multiplies by for "/ 6.0"
+  uint32_t sf = 0;
+  if (r < p.rows && c < p.cols) {
+    float v[16];
+    load16<kInDtype>(p.x, r * p.k + c * 16, v);
+    // amax over finite values; `inf_nan` becomes NaN if any element is Inf or NaN (x * 0). The
+    // reference's scale is then NaN either way (NaN amax, or Inf / 6 overflowing E4M3).
+    float amax = 0.0f, inf_nan = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = __fmul_rn(v[i], gs);
+      amax = fmaxf(amax, fabsf(v[i]));
+      inf_nan = __fmaf_rn(v[i], 0.0f, inf_nan);
+    }
+    const float s = p.div_mode == 0 ? __fmul_rn(amax, inv6) : __fdiv_rn(amax, 6.0f);
+    sf = inf_nan != 0.0f ? 0x7Fu : f32_to_e4m3_rn(s);
+    const float denom = e4m3_to_f32(sf);
+    // else q = 0 for every element: code 0 (a NaN scale included)
+    const uint2 codes = denom > 0.0f ? e2m1_pack16(v, denom, __frcp_rn(denom)) : make_uint2(0u, 0u);
+    *reinterpret_cast<uint2*>(p.packed + r * (p.k >> 1) + c * 8) = codes;
+    if (p.sf_lin != nullptr) p.sf_lin[r * p.cols + c] = static_cast<uint8_t>(sf);
+  }
+  p.sf_swz[sf_swizzle_offset(r, c, c4)] = static_cast<uint8_t>(sf);
+}
+
 template <int kInDtype>
 __global__ void __launch_bounds__(256) nvfp4_quantize_kernel(const QuantParams p) {
   const float gs = resolve_global_scale(p);
   if (p.gs_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.gs_out = gs;
-  const float inv6 = 0.166666672f;  // fl(1/6): what torch on CUDA multiplies by for "/ 6.0"
   const int64_t total = p.rows_pad * p.cols_pad;
   const int64_t c4 = p.cols_pad >> 2;
   // Block (r, c) of the padded scale grid, advanced by the grid stride without dividing.
@@ -221,28 +251,84 @@ __global__ void __launch_bounds__(256) nvfp4_quantize_kernel(const QuantParams p
   const int64_t dr = stride / p.cols_pad, dc = stride - dr * p.cols_pad;
   int64_t r = b0 / p.cols_pad, c = b0 - r * p.cols_pad;
   for (int64_t b = b0; b < total; b += stride) {
-    uint32_t sf = 0;
-    if (r < p.rows && c < p.cols) {
-      float v[16];
-      load16<kInDtype>(p.x, r * p.k + c * 16, v);
-      // amax over finite values; `inf_nan` becomes NaN if any element is Inf or NaN (x * 0). The
-      // reference's scale is then NaN either way (NaN amax, or Inf / 6 overflowing E4M3).
-      float amax = 0.0f, inf_nan = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] = __fmul_rn(v[i], gs);
-        amax = fmaxf(amax, fabsf(v[i]));
-        inf_nan = __fmaf_rn(v[i], 0.0f, inf_nan);
-      }
-      const float s = p.div_mode == 0 ? __fmul_rn(amax, inv6) : __fdiv_rn(amax, 6.0f);
-      sf = inf_nan != 0.0f ? 0x7Fu : f32_to_e4m3_rn(s);
-      const float denom = e4m3_to_f32(sf);
-      // else q = 0 for every element: code 0 (a NaN scale included)
-      const uint2 codes = denom > 0.0f ? e2m1_pack16(v, denom, __frcp_rn(denom)) : make_uint2(0u, 0u);
-      *reinterpret_cast<uint2*>(p.packed + r * (p.k >> 1) + c * 8) = codes;
-      if (p.sf_lin != nullptr) p.sf_lin[r * p.cols + c] = static_cast<uint8_t>(sf);
+    quantize_block<kInDtype>(p, gs, r, c, c4);
+    c += dc;
+    r += dr;
+    if (c >= p.cols_pad) {
+      c -= p.cols_pad;
+      ++r;
     }
-    p.sf_swz[sf_swizzle_offset(r, c, c4)] = static_cast<uint8_t>(sf);
+  }
+}
+
+// Activation quantiser for an LLM projection call, as two launches chained by programmatic
+// dependent launch (each lets the next kernel in the stream start as its first instruction):
+//   nvfp4_act_amax_kernel      every CTA writes the max |x| bits of its grid-stride share to
+//                              parts[blockIdx.x] (no atomics, so nothing needs zeroing first);
+//   nvfp4_act_quantize_kernel  waits for the amax kernel, reduces the partial maxima in every CTA,
+//                              derives gs = 2688 / amax with the same rule as gs_mode 2 and, in
+//                              CTA 0, writes gs and the GEMM alpha 1 / (gs * gs_other); then the
+//                              grid-stride quantisation of nvfp4_quantize_kernel.
+// A weight-streaming GEMM launched after them with programmatic dependent launch starts reading
+// its weights while these run.
+constexpr int kActThreads = 256;
+constexpr int kActMaxParts = 1024;
+
+template <int kInDtype>
+__global__ void __launch_bounds__(kActThreads) nvfp4_act_amax_kernel(const void* x, int64_t numel, uint32_t* parts) {
+  __shared__ uint32_t warp_max[kActThreads / 32];
+  griddep_launch_dependents();
+  uint32_t m = 0;
+  const int64_t nvec = numel >> 4;  // numel is a multiple of 16
+  for (int64_t b = static_cast<int64_t>(blockIdx.x) * kActThreads + threadIdx.x; b < nvec;
+       b += static_cast<int64_t>(gridDim.x) * kActThreads) {
+    float v[16];
+    load16<kInDtype>(x, b * 16, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t w = threadIdx.x < kActThreads / 32 ? warp_max[threadIdx.x] : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w = max(w, __shfl_xor_sync(0xffffffffu, w, o));
+    if (threadIdx.x == 0) parts[blockIdx.x] = w;
+  }
+}
+
+template <int kInDtype>
+__global__ void __launch_bounds__(kActThreads)
+    nvfp4_act_quantize_kernel(const QuantParams p, const uint32_t* parts, int n_parts, const float* gs_other,
+                              float* alpha_out) {
+  __shared__ uint32_t warp_max[kActThreads / 32];
+  griddep_launch_dependents();
+  griddep_wait();  // the amax kernel has finished and its parts are visible
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < n_parts; i += kActThreads) m = max(m, parts[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  uint32_t bits = 0;
+#pragma unroll
+  for (int w = 0; w < kActThreads / 32; ++w) bits = max(bits, warp_max[w]);
+  const float amax = __uint_as_float(bits);
+  const float gs = (amax > 0.0f && amax <= 3.402823466e38f) ? __fdiv_rn(2688.0f, amax) : 1.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (p.gs_out != nullptr) *p.gs_out = gs;
+    if (alpha_out != nullptr) *alpha_out = __frcp_rn(__fmul_rn(gs, *gs_other));
+  }
+  const int64_t total = p.rows_pad * p.cols_pad;
+  const int64_t c4 = p.cols_pad >> 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t dr = stride / p.cols_pad, dc = stride - dr * p.cols_pad;
+  int64_t r = b0 / p.cols_pad, c = b0 - r * p.cols_pad;
+  for (int64_t b = b0; b < total; b += stride) {
+    quantize_block<kInDtype>(p, gs, r, c, c4);
     c += dc;
     r += dr;
     if (c >= p.cols_pad) {

@@ -98,11 +98,14 @@ PRESETS = {
 }
 
 
-# B200 retune for skinny GEMMs (M <= 128, e.g. LLM projections on a few tokens): one-CTA 128x256
-# tiles. A 256-row CTA-pair tile would be at least half empty, and the 128-row tiles keep more SMs
-# streaming B. At M=128, N=28672, K=8192 this is 33 us against 41 us for the pair kernel.
-SKINNY = Config.make(tile=(128, 256))
-SKINNY_MAX_M = 128
+# B200 retune for skinny GEMMs (M <= 128, e.g. LLM projections on a few tokens): the
+# weight-streaming kernel, tile (128, 128). B's rows fill the tensor core's M dimension in 128-row
+# tiles and all of A's rows form its N, so every SM streams its own rows of B once (N/128 tiles
+# instead of N/256) and no MMA work goes to absent rows of A. The one-CTA 128x256 tile
+# (tile=(128, 256)) remains available; a 256-row CTA-pair tile would be at least half empty.
+STREAM_MAX_M = 128
+SKINNY = Config.make(tile=(128, 128))
+SKINNY_MAX_M = STREAM_MAX_M
 
 
 def config_for(m: int, n: int, k: int) -> Config:

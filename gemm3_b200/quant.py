@@ -141,3 +141,42 @@ def dequantize_nvfp4(packed, sf_linear, global_scale: float = 1.0):
         )
     _lib.check(rc, "nvfp4_dequantize")
     return out.to(home)
+
+
+def quantize_nvfp4_act(x, gs_other=None):
+    """Quantize activations with their tensor-wide global scale, for an LLM projection call.
+
+    Same result, bit for bit, as quantize_nvfp4_global(x) (without the linear scales). Two
+    kernels chained by programmatic dependent launch: per-CTA partial maxima, then the
+    quantiser, which also derives gs = 6 * 448 / amax and, if gs_other (a one-element float32
+    CUDA tensor, e.g. the weight's global scale) is given, the GEMM alpha = 1 / (gs * gs_other).
+    A weight-streaming GEMM launched next can start reading its weights while they run (see
+    linear.nvfp4_linear).
+
+    Returns:
+        (packed, sf_swizzled, global_scale, alpha): alpha is None without gs_other.
+    """
+    if x.device.type != "cuda":
+        raise ValueError("quantize_nvfp4_act needs a CUDA tensor")
+    rows, k = x.shape
+    if k % SF_VEC:
+        raise ValueError("K must be a multiple of 16")
+    dev = x.device
+    src = (x if x.dtype in _IN_DTYPES else x.float()).contiguous()
+    packed = torch.empty(rows, k // 2, dtype=torch.uint8, device=dev)
+    sf_swz = torch.empty(sf_swizzled_size(rows, k), dtype=torch.uint8, device=dev)
+    gs = torch.empty(1, dtype=torch.float32, device=dev)
+    ws = torch.empty(_lib.ACT_WORKSPACE_BYTES // 4, dtype=torch.int32, device=dev)
+    alpha = None
+    other = None
+    if gs_other is not None:
+        other = gs_other.reshape(1).to(device=dev, dtype=torch.float32)
+        alpha = torch.empty(1, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().nvfp4_quantize_act(
+            src.data_ptr(), _IN_DTYPES[src.dtype], rows, k, other.data_ptr() if other is not None else None,
+            gs.data_ptr(), alpha.data_ptr() if alpha is not None else None, packed.data_ptr(), sf_swz.data_ptr(),
+            ws.data_ptr(), _stream(dev),
+        )
+    _lib.check(rc, "nvfp4_quantize_act")
+    return packed, sf_swz, gs, alpha

@@ -49,13 +49,15 @@ enum { NVFP4_L2_NORMAL = 0, NVFP4_L2_EVICT_FIRST = 1, NVFP4_L2_EVICT_LAST = 2 };
 
 /*
  * Launch configuration of the GEMM kernel. Zero-initialise and set struct_size; zero fields take
- * their defaults. Mirrors the attributes of nvfp4_gemm_cute.presets.Config
+ * their defaults. The library reads the first struct_size bytes, so a caller built against an
+ * older, shorter struct gets defaults for the fields added since. Mirrors the attributes of nvfp4_gemm_cute.presets.Config
  * (nvfp4_gemm_cute/presets.py:14-35, api.py:20-39) that have a meaning on B200.
  */
 typedef struct nvfp4_gemm_config {
   int32_t struct_size;           /* sizeof(nvfp4_gemm_config) */
   int32_t tile_m;                /* 256 (or 0): CTA pairs, 256x256 tiles; 128: one CTA per 128x256 tile */
-  int32_t tile_n;                /* 256 (only value in this version); 0 = 256 */
+  int32_t tile_n;                /* 256 (or 0); 128 with tile_m 128: weight-streaming kernel for M <= 128,
+                                    128 rows of B (columns of C) per tile, all of A's rows in the MMA's N */
   int32_t raster_band;           /* 128-row tiles per raster band (0 or 1: bands of one tile) */
   int32_t raster_along_m;        /* 0: bands of M-tiles, sweep N ("N sweep"); 1: bands of N-tiles */
   int32_t l2_policy_a;           /* NVFP4_L2_* for A loads */
@@ -66,6 +68,10 @@ typedef struct nvfp4_gemm_config {
   int32_t epi_store_pace_ns;     /* pause between output 32-column chunks (0 = none) */
   int32_t tma_b_first;           /* issue the B load before A in each stage */
   int32_t max_ctas;              /* cap on persistent CTAs (0 = one per SM) */
+  int32_t pdl;                   /* programmatic dependent launch, weight-streaming kernel only (others
+                                    launch plainly): 0 off; 1 every load waits for the preceding kernel;
+                                    2 B and its scales are loaded before that wait, A, its scales and
+                                    alpha after it (B must not be written by the preceding kernel) */
 } nvfp4_gemm_config;
 
 /*
@@ -103,6 +109,29 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
 int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, float global_scale,
                    const float* gs_dev, int32_t gs_mode, int32_t div_mode, void* packed,
                    void* sf_swizzled, void* sf_linear, float* gs_out, void* stream);
+
+/* Device workspace that nvfp4_quantize_act needs (per-CTA partial maxima; overwritten). */
+#define NVFP4_ACT_WORKSPACE_BYTES 4096
+
+/*
+ * Quantise activations x [rows, K] with their tensor-wide global scale for an LLM projection
+ * call: two launches on `stream` (an amax pass writing per-CTA partial maxima to `workspace`,
+ * then the quantiser), chained by programmatic dependent launch. Equivalent, bit for bit, to
+ * nvfp4_amax followed by nvfp4_quantize with gs_mode 2 and div_mode 0:
+ *   gs = 2688 / amax(|x|) (1 if amax is 0, Inf or NaN), written to *gs_out when gs_out != NULL;
+ *   packed codes [rows, K/2] and swizzled scales as nvfp4_quantize writes them.
+ * It replaces the reference's quantize_nvfp4(x, global_scale=gs) (nvfp4_gemm_cute/quant.py:41-59)
+ * with the global-scale recipe of nvfp4_gemm_cute/docs/usage.md:14, and also writes
+ *   *alpha_out = 1 / (gs * *gs_other)  (FP32, correctly rounded)
+ * when alpha_out != NULL: the GEMM alpha for weights quantised with global scale *gs_other (a
+ * device float). workspace: NVFP4_ACT_WORKSPACE_BYTES of device memory, 4-byte aligned, not
+ * shared with a concurrent call. Both kernels let the next launch in the stream start early: a
+ * following nvfp4_gemm_run with cfg->pdl = 2 streams its weights while they run and waits for
+ * them before reading A, A's scales or alpha.
+ */
+int nvfp4_quantize_act(const void* x, int32_t in_dtype, int64_t rows, int64_t k, const float* gs_other,
+                       float* gs_out, float* alpha_out, void* packed, void* sf_swizzled, void* workspace,
+                       void* stream);
 
 /*
  * amax_out[0] = max |x| over numel elements (NaN propagates). No counterpart in the reference

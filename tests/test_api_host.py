@@ -1,6 +1,7 @@
 """CPU: host-side behaviour of the drop-in API — validation before any GPU work, with the
 reference's messages (nvfp4_gemm_cute tests/test_gemm.py:51-142, api.py:67-207)."""
 
+import ctypes
 from dataclasses import replace
 
 import pytest
@@ -31,7 +32,7 @@ def test_config_make_and_presets():
     assert c.attrs == (("fast_swz", 4), ("l2_policy_a", "evict_last"))
     assert Config.make(fallback=None).fallback is None
     assert config_for(1024, 2048, 4096) == g3.DEFAULT
-    assert config_for(16, 28672, 8192).tile == (128, 256)  # B200 skinny retune for M <= 128
+    assert config_for(16, 28672, 8192).tile == (128, 128)  # B200 weight-streaming kernel for M <= 128
     assert config_for(129, 28672, 8192) == g3.DEFAULT
     for size in (4096, 8192, 16384, 32768):
         assert config_for(size, size, size) is g3.PRESETS[(size, size, size)]
@@ -117,3 +118,29 @@ def test_l2_policy_names():
 def test_cpu_operands_rejected_after_guards():
     with pytest.raises(ValueError, match="CUDA"):
         g3.gemm(_expanded(128, 64), _expanded(128, 64), SF, SF)
+
+
+def test_stream_tile_needs_skinny_m():
+    """tile (128, 128) (weight-streaming kernel) holds all of A's rows in one MMA: M <= 128."""
+    a = torch.empty(1, dtype=torch.uint8).expand(129, 64)
+    b = torch.empty(1, dtype=torch.uint8).expand(128, 64)
+    sf = torch.empty(1, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="M <= 128"):
+        g3.gemm(a, b, sf, sf, config=Config.make(tile=(128, 128)))
+    with pytest.raises(ValueError, match="unsupported tile"):
+        g3.gemm(a, b, sf, sf, config=Config.make(tile=(64, 128)))
+
+
+def test_quantize_act_validation_before_gpu():
+    from gemm3_b200 import _lib, build
+
+    build.build()
+    L = _lib.lib()
+    p = ctypes.c_void_p(1 << 20)  # never dereferenced: validation answers first
+    assert L.nvfp4_quantize_act(p, 1, 4, 24, None, None, None, p, p, p, None) == _lib.ERR_INVALID_VALUE  # K % 16
+    # alpha needs the other operand's global scale; the workspace is required
+    assert L.nvfp4_quantize_act(p, 1, 4, 64, None, None, p, p, p, p, None) == _lib.ERR_INVALID_VALUE
+    assert L.nvfp4_quantize_act(p, 1, 4, 64, None, None, None, p, p, None, None) == _lib.ERR_INVALID_VALUE
+    assert L.nvfp4_quantize_act(p, 1, 4, 64, None, None, None, p, p, ctypes.c_void_p((1 << 20) + 2), None) == (
+        _lib.ERR_MISALIGNED
+    )

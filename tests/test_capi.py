@@ -68,7 +68,12 @@ def test_argument_validation_without_gpu(L):
 
 
 def test_config_struct_layout():
-    assert ctypes.sizeof(_lib.GemmConfig) == 13 * 4
+    """The ctypes mirror lists the header's int32 fields in the header's order."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    body = re.search(r"typedef struct nvfp4_gemm_config \{(.*?)\} nvfp4_gemm_config;", text, flags=re.S).group(1)
+    fields = re.findall(r"int32_t\s+(\w+);", body)
+    assert [f for f, _ in _lib.GemmConfig._fields_] == fields
+    assert ctypes.sizeof(_lib.GemmConfig) == 4 * len(fields)
 
 
 def test_cublaslt_adapter_exports_its_header():
