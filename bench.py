@@ -388,6 +388,7 @@ def run_ours(args):
     allgather = None
     if args.allgather and world > 1:
         allgather = time_allgather(c, world, dev)
+        allgather["fused"] = time_fused_gather(sets, world, dev, M, N, K, out_dtype, cfg)
 
     vendor = None
     if world == 1 and not args.no_vendor:
@@ -481,6 +482,61 @@ def time_allgather(c, world, dev):
     return {"ms": gather_ms, "relayout_ms": relayout_ms, "bytes_gathered": nbytes,
             "bus_gbs": nbytes * (world - 1) / world / (gather_ms * 1e-3) / 1e9,
             "layout": "NCCL all-gather to [world*M][N/world], then one copy to row-major [M][N]"}
+
+
+def time_fused_gather(sets, world, dev, M, N, K, out_dtype, cfg):
+    """The gather fused into the GEMM (gemm3_b200.dist.gemm_column_parallel_gather): each rank's
+    epilogue stores its [M, N] block into every rank's row-major [M, world * N] buffer over NVLink,
+    then a one-element all-reduce orders the readers. Device time per step against the plain GEMM
+    on the same inputs, max over ranks; eager launches."""
+    import torch
+    import torch.distributed as dist
+
+    import gemm3_b200 as g3
+    from gemm3_b200 import dist as g3dist
+
+    pg = g3dist.PeerGather(M, world * N, dtype=out_dtype)
+    c = torch.empty(M, N, dtype=out_dtype, device=dev)
+    try:
+        def plain(i):
+            a_q, b_q, a_sf, b_sf, alpha = sets[i % len(sets)]
+            g3.gemm(a_q, b_q, a_sf, b_sf, alpha=alpha, out=c, out_dtype=out_dtype, config=cfg)
+
+        def fused(i):
+            a_q, b_q, a_sf, b_sf, alpha = sets[i % len(sets)]
+            g3dist.gemm_column_parallel_gather(a_q, b_q, a_sf, b_sf, pg, alpha=alpha, out_dtype=out_dtype, config=cfg)
+
+        reps = 10
+        for i in range(3):
+            plain(i)
+            fused(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        for i in range(reps):
+            plain(i)
+        ev[1].record()
+        for i in range(reps):
+            fused(i)
+        ev[2].record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps], dtype=torch.float64,
+                          device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        plain_ms, fused_ms = ms.tolist()
+        status = g3.device_status()
+        if status:
+            raise RuntimeError(f"device status {status} in the fused gather")
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        pg.close()
+        dist.barrier()
+    peer_bytes = M * N * c.element_size() * (world - 1)
+    return {"gemm_ms": plain_ms, "gemm_gather_ms": fused_ms, "extra_ms": fused_ms - plain_ms,
+            "bytes_to_peers_per_rank": peer_bytes,
+            "layout": "row-major [M, world*N] on every rank, written by the GEMM epilogue (peer stores)"}
 
 
 def time_cublaslt(sets, out_dtype, dev, M, N, K):

@@ -20,6 +20,8 @@ ERR_TOO_LARGE = 6
 
 NOALLOC_MAX_ELEMENTS = 1 << 31
 ACT_WORKSPACE_BYTES = 4096
+MAX_GATHER_DST = 8
+IPC_HANDLE_BYTES = 64
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 L2_NORMAL, L2_EVICT_FIRST, L2_EVICT_LAST = 0, 1, 2
@@ -39,6 +41,10 @@ EXPORTED_SYMBOLS = (
     "nvfp4_quantize_global_noalloc",
     "nvfp4_selftest_wait_timeout",
     "nvfp4_quantize_act",
+    "nvfp4_gemm_run_gather",
+    "nvfp4_ipc_get_handle",
+    "nvfp4_ipc_open",
+    "nvfp4_ipc_close",
 )
 
 
@@ -91,6 +97,14 @@ _SIGNATURES = {
     "nvfp4_quantize_global_noalloc": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "nvfp4_selftest_wait_timeout": (ctypes.c_int, [_vp, _i32, _vp]),
     "nvfp4_quantize_act": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "nvfp4_gemm_run_gather": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, ctypes.POINTER(_vp), _i32, _i64, _i64, _vp, _i64, _i64, _i64, _i32,
+         ctypes.POINTER(GemmConfig), _vp, _vp],
+    ),
+    "nvfp4_ipc_get_handle": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(_i64)]),
+    "nvfp4_ipc_open": (ctypes.c_int, [_vp, _i64, ctypes.POINTER(_vp)]),
+    "nvfp4_ipc_close": (ctypes.c_int, [_vp, _i64]),
 }
 
 

@@ -69,6 +69,20 @@ int device_cache(int dev, DeviceCache** out) {
   return NVFP4_OK;
 }
 
+typedef CUresult (*PFN_addr_range)(CUdeviceptr*, size_t*, CUdeviceptr);
+PFN_addr_range g_addr_range = nullptr;
+
+int get_address_range() {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_addr_range != nullptr) return NVFP4_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  G3_CUDA(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
+  if (fn == nullptr || q != cudaDriverEntryPointSuccess) return NVFP4_ERR_UNSUPPORTED;
+  g_addr_range = reinterpret_cast<PFN_addr_range>(fn);
+  return NVFP4_OK;
+}
+
 int get_encoder() {
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_encode != nullptr) return NVFP4_OK;
@@ -183,11 +197,29 @@ __global__ void wait_timeout_selftest_kernel(int* status, int code) {
   }
 }
 
+// Where the epilogue writes C: a row-major view with row stride ldc starting at column col0 of
+// `c`, and optionally the same view in other GPUs' buffers (the fused gather).
+struct OutputSpec {
+  void* c = nullptr;
+  int64_t ldc = 0, col0 = 0;
+  int n_peer = 0;
+  void* peer[g3::kMaxPeers] = {};
+};
+
+template <typename P>
+void set_output(P& p, const OutputSpec& o) {
+  p.c = o.c;
+  p.ldc = o.ldc;
+  p.col0 = o.col0;
+  p.n_peer = o.n_peer;
+  for (int d = 0; d < g3::kMaxPeers; ++d) p.peer[d] = d < o.n_peer ? o.peer[d] : nullptr;
+}
+
 // Weight-streaming kernel (gemm_stream_kernel.cuh) for M <= 128: B in 128-row tiles over a
 // persistent grid of at most one CTA per SM, all of A in the MMA's N dimension.
-int launch_stream(const void* a, const void* b, const void* sfa, const void* sfb, void* c, const float* alpha,
-                  int64_t m, int64_t n, int64_t k, int32_t out_dtype, const nvfp4_gemm_config& def, int32_t* status,
-                  void* stream) {
+int launch_stream(const void* a, const void* b, const void* sfa, const void* sfb, const OutputSpec& out,
+                  const float* alpha, int64_t m, int64_t n, int64_t k, int32_t out_dtype, const nvfp4_gemm_config& def,
+                  int32_t* status, void* stream) {
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != NVFP4_OK) return rc;
@@ -217,7 +249,7 @@ int launch_stream(const void* a, const void* b, const void* sfa, const void* sfb
   g3::StreamParams p;
   p.sfa = static_cast<const uint8_t*>(sfa);
   p.sfb = static_cast<const uint8_t*>(sfb);
-  p.c = c;
+  set_output(p, out);
   p.alpha = alpha;
   p.status = status;
   p.m = static_cast<int>(m);
@@ -341,14 +373,14 @@ int nvfp4_max_active_clusters(int32_t cluster_size, int32_t* out) {
   return NVFP4_OK;
 }
 
-int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sfb, void* c, const float* alpha,
-                   int64_t m, int64_t n, int64_t k, int32_t out_dtype, const nvfp4_gemm_config* cfg, int32_t* status,
-                   void* stream) {
-  if (!a || !b || !sfa || !sfb || !c || !alpha) return NVFP4_ERR_INVALID_VALUE;
+static int gemm_run_impl(const void* a, const void* b, const void* sfa, const void* sfb, const OutputSpec& out,
+                         const float* alpha, int64_t m, int64_t n, int64_t k, int32_t out_dtype,
+                         const nvfp4_gemm_config* cfg, int32_t* status, void* stream) {
+  if (!a || !b || !sfa || !sfb || !out.c || !alpha) return NVFP4_ERR_INVALID_VALUE;
   if (m < 1 || n < 64 || k < 64 || n % 64 || k % 64) return NVFP4_ERR_INVALID_VALUE;
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2) return NVFP4_ERR_INVALID_VALUE;
   if (out_dtype != NVFP4_DTYPE_F16 && out_dtype != NVFP4_DTYPE_BF16) return NVFP4_ERR_INVALID_VALUE;
-  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 16) || !aligned(sfb, 16) || !aligned(c, 32) ||
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(sfa, 16) || !aligned(sfb, 16) || !aligned(out.c, 32) ||
       !aligned(alpha, 4))
     return NVFP4_ERR_MISALIGNED;
   nvfp4_gemm_config def = {};
@@ -364,7 +396,7 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   if (def.pdl < 0 || def.pdl > 2) return NVFP4_ERR_INVALID_VALUE;
   if (def.tile_n == 128) {
     if (def.tile_m != 128 || m > g3::kStreamMaxM) return NVFP4_ERR_INVALID_VALUE;
-    return launch_stream(a, b, sfa, sfb, c, alpha, m, n, k, out_dtype, def, status, stream);
+    return launch_stream(a, b, sfa, sfb, out, alpha, m, n, k, out_dtype, def, status, stream);
   }
   const bool pair = def.tile_m != 128;
   if (def.raster_band < 0) return NVFP4_ERR_INVALID_VALUE;
@@ -397,7 +429,7 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   g3::GemmParams p;
   p.sfa = static_cast<const uint8_t*>(sfa);
   p.sfb = static_cast<const uint8_t*>(sfb);
-  p.c = c;
+  set_output(p, out);
   p.alpha = alpha;
   p.status = status;
   p.m = static_cast<int>(m);
@@ -421,6 +453,7 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
   p.pol_sfa = def.l2_policy_sfa;
   p.pol_sfb = def.l2_policy_sfb;
   p.store_evict_first = def.store_evict_first == 0 ? (k >= 8192) : (def.store_evict_first == 1);
+  if (out.n_peer > 0) p.store_evict_first = 0;  // the rows are read back at once for the peers
   p.pace_ns = def.epi_store_pace_ns;
   p.tma_b_first = def.tma_b_first;
 
@@ -457,6 +490,64 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
       g3::nvfp4_gemm_kernel<false><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
   }
   G3_CUDA(cudaGetLastError());
+  return NVFP4_OK;
+}
+
+int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sfb, void* c, const float* alpha,
+                   int64_t m, int64_t n, int64_t k, int32_t out_dtype, const nvfp4_gemm_config* cfg, int32_t* status,
+                   void* stream) {
+  OutputSpec o;
+  o.c = c;
+  o.ldc = n;
+  return gemm_run_impl(a, b, sfa, sfb, o, alpha, m, n, k, out_dtype, cfg, status, stream);
+}
+
+int nvfp4_gemm_run_gather(const void* a, const void* b, const void* sfa, const void* sfb, void* const* c_dst,
+                          int32_t n_dst, int64_t ldc, int64_t col0, const float* alpha, int64_t m, int64_t n, int64_t k,
+                          int32_t out_dtype, const nvfp4_gemm_config* cfg, int32_t* status, void* stream) {
+  if (c_dst == nullptr || n_dst < 1 || n_dst > NVFP4_MAX_GATHER_DST) return NVFP4_ERR_INVALID_VALUE;
+  if (col0 < 0 || ldc < col0 + n || ldc % 16 || col0 % 16) return NVFP4_ERR_INVALID_VALUE;
+  OutputSpec o;
+  o.c = c_dst[0];
+  o.ldc = ldc;
+  o.col0 = col0;
+  o.n_peer = n_dst - 1;
+  for (int d = 1; d < n_dst; ++d) {
+    if (c_dst[d] == nullptr) return NVFP4_ERR_INVALID_VALUE;
+    if (!aligned(c_dst[d], 16)) return NVFP4_ERR_MISALIGNED;
+    o.peer[d - 1] = c_dst[d];
+  }
+  return gemm_run_impl(a, b, sfa, sfb, o, alpha, m, n, k, out_dtype, cfg, status, stream);
+}
+
+int nvfp4_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return NVFP4_ERR_INVALID_VALUE;
+  int rc = get_address_range();
+  if (rc != NVFP4_OK) return rc;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return NVFP4_ERR_INVALID_VALUE;
+  cudaIpcMemHandle_t h;
+  G3_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  static_assert(sizeof(cudaIpcMemHandle_t) == NVFP4_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return NVFP4_OK;
+}
+
+int nvfp4_ipc_open(const void* handle, int64_t offset, void** ptr) {
+  if (handle == nullptr || ptr == nullptr || offset < 0) return NVFP4_ERR_INVALID_VALUE;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  G3_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return NVFP4_OK;
+}
+
+int nvfp4_ipc_close(void* ptr, int64_t offset) {
+  if (ptr == nullptr || offset < 0) return NVFP4_ERR_INVALID_VALUE;
+  G3_CUDA(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset));
   return NVFP4_OK;
 }
 

@@ -54,10 +54,20 @@ constexpr int kOffAbort = kOffTmemSlot + 4;
 constexpr int kSmemUsed = kOffAbort + 4;
 constexpr int kGemmSmemBytes = kSmemUsed + 1024;  // slack to align the base to 1024 bytes
 
+// Output addressing shared by the kernels: C is a row-major view with row stride `ldc` elements
+// starting at column `col0` of the buffer at `c`. With n_peer > 0 every tile is also stored, at
+// the same offset, into peer[0..n_peer) (other GPUs' buffers mapped into this process, reached
+// over NVLink with plain 16-byte stores): the gather of a column-parallel GEMM fused into the
+// epilogue. n_peer = 0, ldc = N, col0 = 0 is the ordinary contiguous [M, N] output.
+constexpr int kMaxPeers = 7;
+
 struct GemmParams {
   const uint8_t* sfa;
   const uint8_t* sfb;
   void* c;
+  int64_t ldc, col0;
+  int n_peer;
+  void* peer[kMaxPeers];
   const float* alpha;
   int* status;
   int m, n, k;
@@ -96,6 +106,31 @@ __device__ __forceinline__ void tile_coord(const GemmParams& p, int t, int& mt, 
     const int cols = min(g, p.n_tiles - band * g);
     nt = band * g + within % cols;
     mt = within / cols;
+  }
+}
+
+// Fused gather: copy the 32 output rows a warp has just stored (row0 .. row0 + 31, columns
+// [0, cols) of the tile at byte offset `off0` of row row0) from this GPU's buffer into every peer
+// buffer. A lane carries 16 bytes, so each warp store writes 512 contiguous bytes of one row over
+// NVLink; per-thread stores of a thread's own row would scatter 16-byte pieces over 32 rows. The
+// rows are read back through L2 (ld.global.cg), two at a time (more would spill registers of the
+// pair kernel).
+__device__ __forceinline__ void copy_rows_to_peers(const GemmParams& p, int row0, int cols, size_t off0, int lane) {
+  const size_t pitch = static_cast<size_t>(p.ldc) * 2;
+  const bool on = lane * 8 < cols;  // 8 columns (16 bytes) per lane
+  const int rows = min(32, p.m - row0);
+  for (int i0 = 0; i0 < rows; i0 += 2) {
+    uint4 v[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      if (on && i0 + i < rows)
+        v[i] = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.c) + off0 + (i0 + i) * pitch) + lane);
+    for (int d = 0; d < p.n_peer; ++d) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (on && i0 + i < rows)
+          reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer[d]) + off0 + (i0 + i) * pitch)[lane] = v[i];
+    }
   }
 }
 
@@ -316,14 +351,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
       const int gm = mt * kTileM + row;
       if (gm < p.m) {
-        uint8_t* rowp = reinterpret_cast<uint8_t*>(p.c) + (static_cast<size_t>(gm) * p.n + static_cast<size_t>(nt) * kTileN) * 2;
+        const size_t off = (static_cast<size_t>(gm) * p.ldc + p.col0 + static_cast<size_t>(nt) * kTileN) * 2;
+        uint8_t* rowp = reinterpret_cast<uint8_t*>(p.c) + off;
         const int cols_left = p.n - nt * kTileN;
 #pragma unroll
         for (int ch = 0; ch < kTileN / 32; ++ch) {
           if (ch * 32 < cols_left) {
             uint32_t v0[8], v1[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 2; ++i) {
               v0[i] = out[ch * 16 + i];
               v1[i] = out[ch * 16 + 8 + i];
             }
@@ -338,9 +374,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      if (p.n_peer > 0) {
+        __threadfence_block();  // this warp's row stores, before its lanes read each other's rows
+        __syncwarp();
+        const int row0 = mt * kTileM + quad * 32;
+        if (row0 < p.m)
+          copy_rows_to_peers(p, row0, min(kTileN, p.n - nt * kTileN),
+                             (static_cast<size_t>(row0) * p.ldc + p.col0 + static_cast<size_t>(nt) * kTileN) * 2, lane);
+      }
     }
   }
 
+  // Peer stores are visible to the other GPUs before this grid is seen as complete.
+  if (p.n_peer > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -420,8 +420,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
       const int gm = mt * kPairTileM + 128 * static_cast<int>(rank) + row;
       if (gm < p.m) {
-        uint8_t* rowp = reinterpret_cast<uint8_t*>(p.c) +
-                        (static_cast<size_t>(gm) * p.n + static_cast<size_t>(nt) * kPairTileN) * 2;
+        const size_t off = (static_cast<size_t>(gm) * p.ldc + p.col0 + static_cast<size_t>(nt) * kPairTileN) * 2;
+        uint8_t* rowp = reinterpret_cast<uint8_t*>(p.c) + off;
         const int cols_left = p.n - nt * kPairTileN;
 #pragma unroll
         for (int ch = 0; ch < kPairTileN / 32; ++ch) {
@@ -443,9 +443,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
         }
       }
+      if (p.n_peer > 0) {
+        __threadfence_block();  // this warp's row stores, before its lanes read each other's rows
+        __syncwarp();
+        const int row0 = mt * kPairTileM + 128 * static_cast<int>(rank) + quad * 32;
+        if (row0 < p.m)
+          copy_rows_to_peers(p, row0, min(kPairTileN, p.n - nt * kPairTileN),
+                             (static_cast<size_t>(row0) * p.ldc + p.col0 + static_cast<size_t>(nt) * kPairTileN) * 2,
+                             lane);
+      }
     }
   }
 
+  // Peer stores are visible to the other GPUs before this grid is seen as complete.
+  if (p.n_peer > 0) __threadfence_system();
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {

@@ -28,7 +28,7 @@
 //               tens of cycles);
 //   warps 4-7   epilogue: thread (quadrant q, lane l) holds column n = 128 t + 32 q + l of C for
 //               every row m; x alpha in FP32, round to FP16/BF16, store C[m, n] (a warp writes
-//               64 contiguous bytes per row m).
+//               64 contiguous bytes per row m), also into peer GPUs' buffers when asked.
 // Each output element is accumulated over k = 0, 64, 128, ... in one MMA chain, in the same
 // order as the other kernels of this library.
 //
@@ -85,6 +85,9 @@ struct StreamParams {
   const uint8_t* sfa;  // A scales (swizzled); only row block 0 exists for M <= 128
   const uint8_t* sfb;  // B scales (swizzled)
   void* c;
+  int64_t ldc, col0;  // output addressing, as in GemmParams
+  int n_peer;
+  void* peer[kMaxPeers];
   const float* alpha;
   int* status;
   int m, n;
@@ -366,7 +369,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     if (p.pdl != 0) griddep_wait();  // alpha may come from the preceding kernel
     const float alpha = *p.alpha;
-    uint16_t* cbase = static_cast<uint16_t*>(p.c);
+
     int lt = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++lt) {
       const uint32_t buf = static_cast<uint32_t>(lt & 1);
@@ -374,7 +377,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       tc_fence_after();
       const int n_idx = t * kStreamTileN + quad * 32 + lane;
       const bool valid = n_idx < p.n;
-      uint16_t* col = cbase + n_idx;
+      const size_t col = static_cast<size_t>(p.col0) + n_idx;  // element offset of C[0, n_idx]
       for (int ch = 0; ch < p.n_mma; ch += 32) {
         uint32_t r[32];
         const uint32_t taddr = tmem + lane_base + buf * kStreamAccCols + static_cast<uint32_t>(ch);
@@ -394,7 +397,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                 bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
               else
                 bits = __half_as_ushort(__float2half_rn(v));
-              col[static_cast<size_t>(ch + i) * p.n] = bits;
+              const size_t e = static_cast<size_t>(ch + i) * p.ldc + col;
+              static_cast<uint16_t*>(p.c)[e] = bits;
+              for (int d = 0; d < p.n_peer; ++d) static_cast<uint16_t*>(p.peer[d])[e] = bits;
             }
           }
         }
@@ -404,6 +409,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
   }
 
+  // Peer stores are visible to the other GPUs before this grid is seen as complete.
+  if (p.n_peer > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -90,6 +90,38 @@ int nvfp4_gemm_run(const void* a, const void* b, const void* sfa, const void* sf
                    const float* alpha, int64_t m, int64_t n, int64_t k, int32_t out_dtype,
                    const nvfp4_gemm_config* cfg, int32_t* status, void* stream);
 
+/* Destinations of nvfp4_gemm_run_gather: this GPU's buffer and up to 7 other GPUs' buffers. */
+#define NVFP4_MAX_GATHER_DST 8
+#define NVFP4_IPC_HANDLE_BYTES 64
+
+/*
+ * Column-parallel GEMM with the gather of C fused into the epilogue. Computes this rank's block
+ * alpha * A . B^T (B holding the rank's N rows) and writes it as columns [col0, col0 + N) of
+ * every row-major [M, ldc] buffer in c_dst[0..n_dst): c_dst[0] on this GPU (32-byte aligned),
+ * c_dst[1..] other GPUs' buffers mapped into this process (nvfp4_ipc_open; 16-byte aligned),
+ * reached with plain 16-byte stores over NVLink. It replaces the all-gather of the [M, N/g]
+ * blocks and their relayout into row-major [M, N] that follow nvfp4_gemm_run on each rank.
+ * Requires ldc >= col0 + N, ldc % 16 == 0, col0 % 16 == 0, 1 <= n_dst <= NVFP4_MAX_GATHER_DST;
+ * other arguments as nvfp4_gemm_run. The kernel ends with a system-scope fence after its peer
+ * stores; readers of a buffer must still be ordered after every rank's call (for example a
+ * collective on each rank's stream after the GEMM). No counterpart in the reference, which is
+ * single-GPU; it is the optional gather of the column-parallel GEMM.
+ */
+int nvfp4_gemm_run_gather(const void* a, const void* b, const void* sfa, const void* sfb, void* const* c_dst,
+                          int32_t n_dst, int64_t ldc, int64_t col0, const float* alpha, int64_t m, int64_t n,
+                          int64_t k, int32_t out_dtype, const nvfp4_gemm_config* cfg, int32_t* status,
+                          void* stream);
+
+/*
+ * CUDA IPC for the gather's destinations (no counterpart in the reference). get_handle exports the
+ * allocation that contains `ptr` (NVFP4_IPC_HANDLE_BYTES into `handle`) and ptr's offset in it;
+ * another process opens it with nvfp4_ipc_open (peer access enabled on demand) and releases the
+ * mapping with nvfp4_ipc_close(ptr, offset).
+ */
+int nvfp4_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+int nvfp4_ipc_open(const void* handle, int64_t offset, void** ptr);
+int nvfp4_ipc_close(void* ptr, int64_t offset);
+
 /*
  * Quantise x [rows, K] (contiguous, in_dtype F16/BF16/F32, 16-byte aligned) to NVFP4.
  * Replaces quantize_nvfp4 (nvfp4_gemm_cute/quant.py:41-59), bit-exact with it:

@@ -91,3 +91,19 @@ def test_cublaslt_adapter_exports_its_header():
     p = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
     assert L.nvfp4_cublaslt_gemm(p, p, p, p, p, 1.0, 128, 100, 128, 0, None, 0, None) == 1  # N % 64
 
+
+
+def test_gather_entry_validates_before_gpu():
+    """nvfp4_gemm_run_gather: destination count, output view and peer alignment are checked
+    before any device access."""
+    build.build()
+    L = _lib.lib()
+    p = ctypes.c_void_p(1 << 20)
+    dst = (ctypes.c_void_p * 2)(1 << 20, (1 << 21) + 8)  # second destination misaligned
+    good = (ctypes.c_void_p * 2)(1 << 20, 1 << 21)
+    run = L.nvfp4_gemm_run_gather
+    assert run(p, p, p, p, good, 0, 256, 0, p, 128, 128, 128, 0, None, None, None) == _lib.ERR_INVALID_VALUE
+    assert run(p, p, p, p, good, 9, 256, 0, p, 128, 128, 128, 0, None, None, None) == _lib.ERR_INVALID_VALUE
+    assert run(p, p, p, p, good, 2, 200, 128, p, 128, 128, 128, 0, None, None, None) == _lib.ERR_INVALID_VALUE
+    assert run(p, p, p, p, good, 2, 264, 8, p, 128, 128, 128, 0, None, None, None) == _lib.ERR_INVALID_VALUE
+    assert run(p, p, p, p, dst, 2, 256, 128, p, 128, 128, 128, 0, None, None, None) == _lib.ERR_MISALIGNED

@@ -73,3 +73,62 @@ def test_column_parallel_gemm_two_gpus(cuda_ext, tmp_path):
     mp.spawn(_nccl_worker, args=(world, _free_port(), 384, 1024, 512, str(tmp_path)), nprocs=world, join=True)
     for r in range(world):
         assert (tmp_path / f"rank{r}").read_text() == "ok", r
+
+
+def _gather_worker(rank, world, port, m, n, k, result_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    import gemm3_b200 as g3
+    from gemm3_b200 import dist as g3dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    gather = None
+    try:
+        g = torch.Generator(device=dev).manual_seed(9)
+        a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+        b_whole = torch.randn(n, k, device=dev, generator=g).to(torch.bfloat16)
+        start, stop = g3dist.shard_bounds(n, world, rank)
+        aq, asf, _, gsa = g3.quantize_nvfp4_global(a)
+        bq_whole, bsf_whole, _, gsb = g3.quantize_nvfp4_global(b_whole)
+        bq, bsf = g3dist.shard_quantized(bq_whole, bsf_whole, world, rank)
+        gather = g3dist.PeerGather(m, n, dtype=torch.bfloat16)
+        ok = True
+        for scale in (1.0, 0.5):  # two calls in a row into the same buffers
+            alpha = (scale / (gsa * gsb)).reshape(1)
+            gather.full.fill_(float("nan"))
+            gather.barrier()  # every rank's buffer reset before any rank writes into it
+            full = g3dist.gemm_column_parallel_gather(aq, bq, asf, bsf, gather, alpha=alpha)
+            want = g3.gemm(aq, bq_whole, asf, bsf_whole, alpha=alpha, out_dtype=torch.bfloat16)
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(full, want)
+        ok = ok and g3.device_status() == 0
+        with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if ok else "mismatch")
+    finally:
+        if gather is not None:
+            gather.barrier()
+            torch.cuda.synchronize()
+            gather.close()
+            dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_fused_gather_two_gpus(cuda_ext, tmp_path):
+    """The gather fused into the GEMM epilogue (peer stores over NVLink into every rank's full-C
+    buffer): after the barrier, each rank's buffer equals the one-GPU GEMM bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    mp.spawn(_gather_worker, args=(world, _free_port(), 320, 1536, 1024, str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        assert (tmp_path / f"rank{r}").read_text() == "ok", r
