@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (ch * 32 < cols_left) {
             uint32_t v0[8], v1[8];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
+            for (int i = 0; i < 8; ++i) {
               v0[i] = out[ch * 16 + i];
               v1[i] = out[ch * 16 + 8 + i];
             }
