@@ -239,10 +239,14 @@ int launch_stream(const void* a, const void* b, const void* sfa, const void* sfb
   {
     std::lock_guard<std::mutex> lock(g_mu);
     if (!d->stream_attr_set) {
-      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   g3::kStreamSmemLimit));
-      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   g3::kStreamSmemLimit));
+      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<true, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kStreamSmemLimit));
+      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<false, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kStreamSmemLimit));
+      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<true, true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kStreamSmemLimit));
+      G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_stream_kernel<false, true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kStreamSmemLimit));
       d->stream_attr_set = true;
     }
   }
@@ -277,10 +281,13 @@ int launch_stream(const void* a, const void* b, const void* sfa, const void* sfb
   attr.val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = &attr;
   lc.numAttrs = def.pdl != 0 ? 1 : 0;
+  const bool view = out.n_peer > 0 || out.ldc != n || out.col0 != 0;
   if (out_dtype == NVFP4_DTYPE_BF16)
-    G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<true>, tmap_a, tmap_b, p));
+    G3_CUDA(view ? cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<true, true>, tmap_a, tmap_b, p)
+                 : cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<true, false>, tmap_a, tmap_b, p));
   else
-    G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<false>, tmap_a, tmap_b, p));
+    G3_CUDA(view ? cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<false, true>, tmap_a, tmap_b, p)
+                 : cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_stream_kernel<false, false>, tmap_a, tmap_b, p));
   return NVFP4_OK;
 }
 

@@ -102,7 +102,9 @@ struct StreamParams {
   int pol_b, pol_sfb;
 };
 
-template <bool kBF16>
+// kOutView: C is a strided view (ldc, col0) and/or also stored into peer buffers (the fused
+// gather); false compiles the contiguous [M, N] store alone.
+template <bool kBF16, bool kOutView>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     nvfp4_gemm_stream_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                              const StreamParams p) {
@@ -369,7 +371,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     if (p.pdl != 0) griddep_wait();  // alpha may come from the preceding kernel
     const float alpha = *p.alpha;
-
     int lt = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++lt) {
       const uint32_t buf = static_cast<uint32_t>(lt & 1);
@@ -377,7 +378,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       tc_fence_after();
       const int n_idx = t * kStreamTileN + quad * 32 + lane;
       const bool valid = n_idx < p.n;
-      const size_t col = static_cast<size_t>(p.col0) + n_idx;  // element offset of C[0, n_idx]
       for (int ch = 0; ch < p.n_mma; ch += 32) {
         uint32_t r[32];
         const uint32_t taddr = tmem + lane_base + buf * kStreamAccCols + static_cast<uint32_t>(ch);
@@ -387,7 +387,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           tmem_ld_32x32b_x16(taddr, r);
         tmem_ld_wait();
         const int rows = min(32, p.m - ch);
-        if (valid) {
+        if (valid && !kOutView) {
+          // contiguous [M, N] output, no peers: C[m, n] = col[m * N]
+          uint16_t* col = static_cast<uint16_t*>(p.c) + n_idx;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             if (i < rows) {
@@ -397,7 +399,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                 bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
               else
                 bits = __half_as_ushort(__float2half_rn(v));
-              const size_t e = static_cast<size_t>(ch + i) * p.ldc + col;
+              col[static_cast<size_t>(ch + i) * p.n] = bits;
+            }
+          }
+        } else if (valid && kOutView) {
+          // strided view and/or the fused gather into the peers' buffers
+          const size_t base = static_cast<size_t>(ch) * p.ldc + p.col0 + n_idx;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i < rows) {
+              const float v = __fmul_rn(__uint_as_float(r[i]), alpha);
+              uint16_t bits;
+              if constexpr (kBF16)
+                bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+              else
+                bits = __half_as_ushort(__float2half_rn(v));
+              const size_t e = base + static_cast<size_t>(i) * p.ldc;
               static_cast<uint16_t*>(p.c)[e] = bits;
               for (int d = 0; d < p.n_peer; ++d) static_cast<uint16_t*>(p.peer[d])[e] = bits;
             }
@@ -410,7 +427,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   }
 
   // Peer stores are visible to the other GPUs before this grid is seen as complete.
-  if (p.n_peer > 0) __threadfence_system();
+  if (kOutView && p.n_peer > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

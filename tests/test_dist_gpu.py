@@ -129,6 +129,8 @@ def test_fused_gather_two_gpus(cuda_ext, tmp_path):
     import torch.multiprocessing as mp
 
     world = 2
-    mp.spawn(_gather_worker, args=(world, _free_port(), 320, 1536, 1024, str(tmp_path)), nprocs=world, join=True)
-    for r in range(world):
-        assert (tmp_path / f"rank{r}").read_text() == "ok", r
+    # M = 320: the CTA-pair kernel; M = 64: the weight-streaming kernel (skinny-M preset)
+    for m in (320, 64):
+        mp.spawn(_gather_worker, args=(world, _free_port(), m, 1536, 1024, str(tmp_path)), nprocs=world, join=True)
+        for r in range(world):
+            assert (tmp_path / f"rank{r}").read_text() == "ok", (m, r)
