@@ -43,6 +43,10 @@ def parse():
     p.add_argument("--steps", type=int, default=3000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--size", type=int, default=8192, help="M = N = K (N is per GPU when --gpus > 1)")
+    p.add_argument("--n-total", type=int, default=0,
+                   help="split this N over the GPUs (strong scaling; BASELINE configs 2 and 3) instead of N = size per GPU")
+    p.add_argument("--outliers", type=float, default=0.0,
+                   help="fraction of A and B entries replaced by +-50 (sigma = 1), e.g. 0.001 for BASELINE config 3")
     p.add_argument("--out-dtype", choices=["bf16", "fp16"], default="bf16")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--allgather", action="store_true")
@@ -59,7 +63,17 @@ def parse():
     p.add_argument("--llm-tile", default="auto", choices=["auto", "256", "128", "stream"])
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.n_total and args.n_total % (args.gpus * 128):
+        p.error(f"--n-total {args.n_total} must split into {args.gpus} blocks of whole 128 rows")
     return args
+
+
+def n_per_gpu(args):
+    return args.n_total // args.gpus if args.n_total else args.size
+
+
+def scaling(args):
+    return "strong" if args.n_total else "weak"
 
 
 def peaks():
@@ -153,7 +167,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    n_total = args.size * args.gpus
+    n_total = n_per_gpu(args) * args.gpus
     base = cpu_baseline(args, args.size, n_total, args.size, seconds=0, steps=args.steps, warmup=args.warmup)
     ms_per_step = base["seconds_total"] / base["samples"] * 1e3
     line = {
@@ -166,7 +180,7 @@ def run_reference(args):
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling(args),
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic: seeded N(0,1) BF16 operands, global scale 2688/amax",
@@ -200,10 +214,11 @@ def profiled_traffic(m, n, k, out_dtype):
 
 def workload_config(args):
     return {
-        "workload": f"NVFP4 GEMM {args.size}x{args.size * args.gpus}x{args.size} "
-                    f"({'BF16' if args.out_dtype == 'bf16' else 'FP16'} out)",
+        "workload": f"NVFP4 GEMM {args.size}x{n_per_gpu(args) * args.gpus}x{args.size} "
+                    f"({'BF16' if args.out_dtype == 'bf16' else 'FP16'} out)"
+                    + (f", {args.outliers:g} of entries +-50 sigma" if args.outliers else ""),
         "m": args.size,
-        "n_per_gpu": args.size,
+        "n_per_gpu": n_per_gpu(args),
         "k": args.size,
         "global_batch": args.size,
         "seq_len": None,
@@ -272,10 +287,11 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------- GPU path
-def make_operands(rows, k, seed, dev, sharded=False):
+def make_operands(rows, k, seed, dev, sharded=False, outliers=0.0):
     """Seeded N(0,1) BF16 -> NVFP4 with the on-device global scale. `sharded`: these rows are
     this rank's block of a tensor split over the process group, quantised with the whole
-    tensor's global scale (one all-reduce of the amax)."""
+    tensor's global scale (one all-reduce of the amax). `outliers`: that fraction of the entries
+    (seeded positions, possibly repeated) becomes +-50 with a random sign."""
     import torch
 
     import gemm3_b200 as g3
@@ -283,6 +299,11 @@ def make_operands(rows, k, seed, dev, sharded=False):
 
     g = torch.Generator(device=dev).manual_seed(seed)
     x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
+    n_out = int(x.numel() * outliers)
+    if n_out:
+        pos = torch.randint(x.numel(), (n_out,), device=dev, generator=g)
+        sign = torch.randint(0, 2, (n_out,), device=dev, generator=g).to(torch.bfloat16) * 2 - 1
+        x.view(-1)[pos] = sign * 50.0
     if sharded:
         q, sf, _, gs = g3dist.quantize_shard_global(x)
     else:
@@ -310,7 +331,8 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     assert g3.supported(), "needs sm_100 and the built extension"
 
-    M = N = K = args.size
+    M = K = args.size
+    N = n_per_gpu(args)
     out_dtype = torch.bfloat16 if args.out_dtype == "bf16" else torch.float16
     sm, _, l2 = g3.hw.device_info(local)
     set_bytes = M * K // 2 + N * K // 2 + (M + N) * K // 16
@@ -318,9 +340,10 @@ def run_ours(args):
     n_sets = min(n_sets, 8)
     sets = []
     for s in range(n_sets):
-        a_q, a_sf, gs_a = make_operands(M, K, seed=1000 * s, dev=dev)  # A replicated: same seed on every rank
+        a_q, a_sf, gs_a = make_operands(M, K, seed=1000 * s, dev=dev, outliers=args.outliers)  # A: same on every rank
         # this rank's block of B (N rows of the N * world), with B's global scale over all ranks
-        b_q, b_sf, gs_b = make_operands(N, K, seed=1000 * s + 1 + 7919 * rank, dev=dev, sharded=world > 1)
+        b_q, b_sf, gs_b = make_operands(N, K, seed=1000 * s + 1 + 7919 * rank, dev=dev, sharded=world > 1,
+                                        outliers=args.outliers)
         alpha = (1.0 / (gs_a * gs_b)).reshape(1).float()
         sets.append((a_q, b_q, a_sf, b_sf, alpha))
     c = torch.empty(M, N, dtype=out_dtype, device=dev)
@@ -417,7 +440,7 @@ def run_ours(args):
         "ms_per_step": ms_per_step,
         "us_per_gemm": launch_ms * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling(args),
         "vs_baseline": None,
         "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 scales) -> fp32 accumulate",
         "data": "synthetic: seeded N(0,1) BF16 quantised to NVFP4, global scale 2688/amax",
