@@ -34,6 +34,7 @@ sys.path.insert(0, REPO)
 
 NOMINAL_FP4_DENSE_TFLOPS = 9000.0
 FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_BF16_SUSTAINED_TFLOPS = 1400.0
 METRIC = "NVFP4 GEMM PFLOP/s per job (2*M*N*K / time)"
 
 
@@ -76,14 +77,18 @@ def scaling(args):
     return "strong" if args.n_total else "weak"
 
 
-def peaks():
+def peaks(sustained=False):
+    """(bf16 TF/s, HBM GB/s, source) from MEASURED_PEAKS.json: the burst bf16 figure for a kernel
+    timed alone, the sustained one (seconds-long loop under the power cap) for a kernel timed
+    inside a long run."""
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return float(d["bf16_tflops"]), float(d.get("hbm_gbs", 0.0)), "measured"
+        key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+        return float(d[key]), float(d.get("hbm_gbs", 0.0)), "measured"
     except (OSError, KeyError, ValueError):
-        return FALLBACK_BF16_TFLOPS, 6650.0, "fallback"
+        return (FALLBACK_BF16_SUSTAINED_TFLOPS if sustained else FALLBACK_BF16_TFLOPS), 6650.0, "fallback"
 
 
 # ----------------------------------------------------------------------------------- CPU path
@@ -372,10 +377,20 @@ def run_ours(args):
         for i in range(args.warmup):
             graphs[i % n_sets].replay()
         torch.cuda.synchronize()
+        cur = torch.cuda.current_stream(dev)
+        # single launches before the long run (burst clocks), each bracketed by events
+        lat = []
+        for i in range(min(args.steps, 32)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            graphs[i % n_sets].replay()
+            e1.record(cur)
+            lat.append((e0, e1))
+        torch.cuda.synchronize()
+        launch_ms = statistics.median(a.elapsed_time(b) for a, b in lat)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        cur = torch.cuda.current_stream(dev)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clocks:
             start.record(cur)
@@ -386,16 +401,6 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
         ms_local = start.elapsed_time(end)
-        # per-launch duration for the roofline: a short event-bracketed run of single replays
-        lat = []
-        for i in range(min(args.steps, 64)):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(cur)
-            graphs[i % n_sets].replay()
-            e1.record(cur)
-            lat.append((e0, e1))
-        torch.cuda.synchronize()
-        launch_ms = statistics.median(a.elapsed_time(b) for a, b in lat)
     status = g3.device_status()
     if status:
         raise RuntimeError(f"device status {status} after timing")
@@ -427,9 +432,13 @@ def run_ours(args):
         cpu = cpu_baseline(args, M, N, K, seconds=args.cpu_seconds, warmup=1)
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
-    bf16_peak, _, peak_src = peaks()
-    fp4_peak = 4.0 * bf16_peak
-    achieved = 2.0 * M * N * K / (launch_ms * 1e-3) / 1e12
+    # The timed region is one GEMM launch per step, back to back for seconds: its average launch
+    # duration is set against the sustained peak; the burst single-launch figure is kept beside.
+    bf16_sus, _, peak_src = peaks(sustained=True)
+    bf16_burst, _, _ = peaks()
+    fp4_peak, fp4_burst = 4.0 * bf16_sus, 4.0 * bf16_burst
+    achieved = 2.0 * M * N * K / (ms_per_step * 1e-3) / 1e12
+    achieved_burst = 2.0 * M * N * K / (launch_ms * 1e-3) / 1e12
     line = {
         "metric": METRIC,
         "value": value,
@@ -452,8 +461,12 @@ def run_ours(args):
             "peak": fp4_peak,
             "unit": "TFLOP/s",
             "frac": achieved / fp4_peak,
-            "peak_source": (f"4 x bf16_tflops of MEASURED_PEAKS.json ({bf16_peak:.0f}); dense FP4 = 4x dense BF16"
-                            if peak_src == "measured" else f"4 x fallback bf16 {bf16_peak:.0f}"),
+            "peak_source": (f"4 x bf16_tflops_sustained of MEASURED_PEAKS.json ({bf16_sus:.0f}); dense FP4 = 4x dense "
+                            f"BF16; achieved = the timed region's average launch ({ms_per_step * 1e3:.1f} us)"
+                            if peak_src == "measured" else f"4 x fallback sustained bf16 {bf16_sus:.0f}"),
+            "burst": {"us_per_launch": launch_ms * 1e3, "achieved": achieved_burst, "peak": fp4_burst,
+                      "frac": achieved_burst / fp4_burst,
+                      "note": "median single launch before the long run, against 4 x bf16_tflops (burst)"},
             "frac_of_nominal_9pf": achieved / NOMINAL_FP4_DENSE_TFLOPS,
             "traffic": profiled_traffic(M, N, K, args.out_dtype),
             "algorithmic_bytes": M * K // 2 + N * K // 2 + (M + N) * K // 16 + 2 * M * N,
@@ -609,6 +622,11 @@ def time_cublaslt(sets, out_dtype, dev, M, N, K):
 
 
 def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):
+    """End to end through the public API from pinned host memory, every step: H2D of that step's
+    BF16 A and B, on-device amax + quantize_nvfp4_global of both, gemm, D2H of C. Steps are
+    software-pipelined over two buffer slots and three streams (H2D, compute, D2H), so the copies
+    of one step overlap the compute of the next and PCIe carries both directions at once; every
+    step's copies still happen inside the timed region. Device time, max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -617,29 +635,54 @@ def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):
     g = torch.Generator().manual_seed(11 + rank)
     a_h = torch.randn(M, K, generator=g).to(torch.bfloat16).pin_memory()
     b_h = torch.randn(N, K, generator=g).to(torch.bfloat16).pin_memory()
-    c_h = torch.empty(M, N, dtype=out_dtype).pin_memory()
-    a_d = torch.empty_like(a_h, device=dev)
-    b_d = torch.empty_like(b_h, device=dev)
-    c_d = torch.empty(M, N, dtype=out_dtype, device=dev)
+    slots = 2
+    c_h = [torch.empty(M, N, dtype=out_dtype).pin_memory() for _ in range(slots)]
+    a_d = [torch.empty_like(a_h, device=dev) for _ in range(slots)]
+    b_d = [torch.empty_like(b_h, device=dev) for _ in range(slots)]
+    c_d = [torch.empty(M, N, dtype=out_dtype, device=dev) for _ in range(slots)]
+    comp = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    h2d_done = [ev() for _ in range(slots)]
+    comp_done = [ev() for _ in range(slots)]
+    d2h_done = [ev() for _ in range(slots)]
+    used = [False] * slots
 
-    def step():
-        a_d.copy_(a_h, non_blocking=True)
-        b_d.copy_(b_h, non_blocking=True)
-        aq, asf, _, gsa = g3.quantize_nvfp4_global(a_d)
-        bq, bsf, _, gsb = g3.quantize_nvfp4_global(b_d)
-        g3.gemm(aq, bq, asf, bsf, alpha=(1.0 / (gsa * gsb)), out=c_d, out_dtype=out_dtype, config=cfg)
-        c_h.copy_(c_d, non_blocking=True)
+    def step(i):
+        s = i % slots
+        with torch.cuda.stream(h2d):
+            if used[s]:
+                h2d.wait_event(comp_done[s])  # the quantiser of step i - slots has read a_d/b_d
+            a_d[s].copy_(a_h, non_blocking=True)
+            b_d[s].copy_(b_h, non_blocking=True)
+            h2d_done[s].record(h2d)
+        comp.wait_event(h2d_done[s])
+        if used[s]:
+            comp.wait_event(d2h_done[s])  # C of step i - slots has left the device
+        aq, asf, _, gsa = g3.quantize_nvfp4_global(a_d[s])
+        bq, bsf, _, gsb = g3.quantize_nvfp4_global(b_d[s])
+        g3.gemm(aq, bq, asf, bsf, alpha=(1.0 / (gsa * gsb)), out=c_d[s], out_dtype=out_dtype, config=cfg)
+        comp_done[s].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(comp_done[s])
+            c_h[s].copy_(c_d[s], non_blocking=True)
+            d2h_done[s].record(d2h)
+        used[s] = True
 
-    for _ in range(2):
-        step()
+    for i in range(2 * slots):
+        step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.e2e_steps):
-        step()
-    e1.record()
+    e0.record(comp)
+    h2d.wait_event(e0)
+    d2h.wait_event(e0)
+    for i in range(args.e2e_steps):
+        step(i)
+    comp.wait_stream(d2h)
+    comp.wait_stream(h2d)
+    e1.record(comp)
     torch.cuda.synchronize()
     ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -650,10 +693,11 @@ def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):
         "value": val,
         "unit": "PFLOP/s",
         "h2d_bytes_per_step": (a_h.numel() + b_h.numel()) * 2,
-        "d2h_bytes_per_step": c_h.numel() * c_h.element_size(),
+        "d2h_bytes_per_step": c_h[0].numel() * c_h[0].element_size(),
         "ms_per_step": ms / args.e2e_steps,
         "steps": args.e2e_steps,
-        "path": "pinned host BF16 A,B -> H2D -> amax + quantize_nvfp4 (GPU) -> gemm -> D2H C",
+        "path": ("pinned host BF16 A,B -> H2D -> amax + quantize_nvfp4 (GPU) -> gemm -> D2H C; "
+                 "two slots, H2D / compute / D2H on three streams"),
     }
 
 
