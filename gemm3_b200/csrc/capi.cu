@@ -672,11 +672,11 @@ int nvfp4_quantize_act(const void* x, int32_t in_dtype, int64_t rows, int64_t k,
     default: g3::nvfp4_act_amax_kernel<2><<<static_cast<int>(parts), g3::kActThreads, 0, s>>>(x, rows * k, ws); break;
   }
   G3_CUDA(cudaGetLastError());
-  // At most one quantiser CTA per SM: they become resident early (programmatic launch) and wait
-  // for the amax kernel, and each SM must keep room for a weight-streaming GEMM CTA (launched
-  // early the same way) beside it.
+  // For the few rows a weight-streaming GEMM follows (<= 128), at most one quantiser CTA per SM:
+  // they become resident early (programmatic launch) and wait for the amax kernel, and each SM
+  // must keep room for a GEMM CTA launched early the same way. Larger inputs get a full wave.
   int qgrid = quant_grid(d, in_dtype, p.rows_pad * p.cols_pad);
-  if (qgrid > d->sm_count) qgrid = d->sm_count;
+  if (rows <= 128 && qgrid > d->sm_count) qgrid = d->sm_count;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(qgrid), 1, 1);
   lc.blockDim = dim3(g3::kActThreads, 1, 1);

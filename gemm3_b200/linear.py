@@ -11,14 +11,15 @@ the previous one ends (programmatic dependent launch):
    waiting and loads x's codes, scales and alpha once step 1 has finished: the weight stream
    from HBM, which sets the call's time, starts while the activations are being quantised.
 
-Larger x goes through quantize_nvfp4_global and the regular gemm preset. The result equals
-quantize_nvfp4_global(x) followed by gemm(...) with alpha = 1 / (gs_x * gs_w), bit for bit.
+Larger x goes through the same activation quantiser and the regular gemm preset. The result
+equals quantize_nvfp4_global(x) followed by gemm(...) with alpha = 1 / (gs_x * gs_w), bit for
+bit.
 """
 
 import torch
 
 from . import api, presets
-from .quant import quantize_nvfp4_act, quantize_nvfp4_global
+from .quant import quantize_nvfp4_act
 
 
 def nvfp4_linear(x, weight, weight_sf, weight_gs, out=None, out_dtype=torch.bfloat16):
@@ -37,6 +38,5 @@ def nvfp4_linear(x, weight, weight_sf, weight_gs, out=None, out_dtype=torch.bflo
     if m <= presets.STREAM_MAX_M:
         xq, xsf, _, alpha = quantize_nvfp4_act(x, weight_gs)
         return api._gemm(xq, weight, xsf, weight_sf, alpha, out, out_dtype, presets.SKINNY, 2)
-    xq, xsf, _, gs_x = quantize_nvfp4_global(x)
-    alpha = torch.reciprocal(gs_x * weight_gs.reshape(1))
+    xq, xsf, _, alpha = quantize_nvfp4_act(x, weight_gs)
     return api.gemm(xq, weight, xsf, weight_sf, alpha=alpha, out=out, out_dtype=out_dtype)
