@@ -150,6 +150,59 @@ __device__ __forceinline__ uint2 e2m1_pack16(const float (&xb)[16], float d, flo
   return make_uint2(e2m1_pack8(xb, d, r, d_lo), e2m1_pack8(xb + 8, d, r, d_lo));
 }
 
+// e2m1_pack8 for a block whose every |xb| is at least 2^-100, in paired FP32 arithmetic (one
+// f32x2 instruction per two elements). There the quotient is the correctly rounded one and is a
+// normal float (|q| >= 2^-109), so the reference's sign test q < 0 is just the sign of xb and of
+// q; the conversions take the signed quotients and set the sign bit themselves (a negative q whose
+// magnitude rounds to 0 gives code 8, as in the reference). lo and hi carry the same sign, so
+// their codes can differ only in the magnitude bits, which the exact steps then replace.
+__device__ __forceinline__ uint32_t e2m1_pack8_signed(const float* xb, float d, float r) {
+  const float2 r2 = make_float2(r, r), nd2 = make_float2(-d, -d);
+  const float2 klo = make_float2(0x1.ffffp-1f, 0x1.ffffp-1f);     // 1 - 2^-17
+  const float2 khi = make_float2(0x1.00008p+0f, 0x1.00008p+0f);   // 1 + 2^-17
+  float q[8], lo[8], hi[8];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const float2 x = make_float2(xb[i], xb[i + 1]);
+    const float2 q1 = __fmul2_rn(x, r2);
+    const float2 rem = __ffma2_rn(q1, nd2, x);
+    const float2 qq = __ffma2_rn(rem, r2, q1);
+    const float2 l = __fmul2_rn(qq, klo), h = __fmul2_rn(qq, khi);
+    q[i] = qq.x;
+    q[i + 1] = qq.y;
+    lo[i] = l.x;
+    lo[i + 1] = l.y;
+    hi[i] = h.x;
+    hi[i + 1] = h.y;
+  }
+  uint32_t w = cvt_e2m1x8(lo);
+  const uint32_t near_tie = w ^ cvt_e2m1x8(hi);
+  if (near_tie != 0u) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((near_tie >> (4 * i)) & 0xFu)
+        w = (w & ~(0x7u << (4 * i))) | (e2m1_mag_code_steps(fabsf(q[i])) << (4 * i));
+  }
+  return w;
+}
+
+// max(a, b, c), NaN if any of them is NaN; min(a, b, c) ignoring NaN (sm_100 three-input forms).
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Byte offset of scale (row, col) in the 128x4 swizzled layout with `c4` 4-column groups.
 __device__ __forceinline__ int64_t sf_swizzle_offset(int64_t row, int64_t col, int64_t c4) {
   return ((row >> 7) * c4 + (col >> 2)) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + (col & 3);
@@ -219,20 +272,36 @@ __device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, i
   if (r < p.rows && c < p.cols) {
     float v[16];
     load16<kInDtype>(p.x, r * p.k + c * 16, v);
-    // amax over finite values; `inf_nan` becomes NaN if any element is Inf or NaN (x * 0). The
-    // reference's scale is then NaN either way (NaN amax, or Inf / 6 overflowing E4M3).
-    float amax = 0.0f, inf_nan = 0.0f;
+    const float2 gs2 = make_float2(gs, gs);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = __fmul_rn(v[i], gs);
-      amax = fmaxf(amax, fabsf(v[i]));
-      inf_nan = __fmaf_rn(v[i], 0.0f, inf_nan);
+    for (int i = 0; i < 16; i += 2) {
+      const float2 xb = __fmul2_rn(make_float2(v[i], v[i + 1]), gs2);
+      v[i] = xb.x;
+      v[i + 1] = xb.y;
     }
+    // amax is NaN if any element is NaN and Inf if one is infinite: the reference's scale is NaN
+    // either way (NaN amax, or Inf / 6 overflowing E4M3), and f32_to_e4m3_rn maps both to 0x7F.
+    // mn, the smallest magnitude, picks the arithmetic below.
+    float amax = max3_nan(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
+    float mn = min3(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
+#pragma unroll
+    for (int i = 3; i < 15; i += 2) {
+      amax = max3_nan(amax, fabsf(v[i]), fabsf(v[i + 1]));
+      mn = min3(mn, fabsf(v[i]), fabsf(v[i + 1]));
+    }
+    amax = max_nan(amax, fabsf(v[15]));
+    mn = fminf(mn, fabsf(v[15]));
     const float s = p.div_mode == 0 ? __fmul_rn(amax, inv6) : __fdiv_rn(amax, 6.0f);
-    sf = inf_nan != 0.0f ? 0x7Fu : f32_to_e4m3_rn(s);
+    sf = f32_to_e4m3_rn(s);
     const float denom = e4m3_to_f32(sf);
-    // else q = 0 for every element: code 0 (a NaN scale included)
-    const uint2 codes = denom > 0.0f ? e2m1_pack16(v, denom, __frcp_rn(denom)) : make_uint2(0u, 0u);
+    // else q = 0 for every element: code 0 (a NaN scale included). Blocks holding a zero or a
+    // magnitude below 2^-100 take the general path, which decides signs without the quotient.
+    uint2 codes = make_uint2(0u, 0u);
+    if (denom > 0.0f) {
+      const float rd = __frcp_rn(denom);
+      codes = mn >= 0x1p-100f ? make_uint2(e2m1_pack8_signed(v, denom, rd), e2m1_pack8_signed(v + 8, denom, rd))
+                              : e2m1_pack16(v, denom, rd);
+    }
     *reinterpret_cast<uint2*>(p.packed + r * (p.k >> 1) + c * 8) = codes;
     if (p.sf_lin != nullptr) p.sf_lin[r * p.cols + c] = static_cast<uint8_t>(sf);
   }
