@@ -41,7 +41,8 @@ struct DeviceCache {
   bool gemm_attr_set = false;
   bool stream_attr_set = false;
   int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
-  int quant_blocks[3] = {0, 0, 0};  // co-resident 256-thread quantiser blocks per SM, per input dtype
+  // co-resident 256-thread quantiser blocks per SM, per input dtype and index width (32 / 64 bits)
+  int quant_blocks[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 };
 DeviceCache g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -161,19 +162,32 @@ int grid_for(int64_t work, int sm_count, int threads = 256) {
   return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
+// The quantiser instantiation for an input dtype and index width: 32-bit indices whenever every
+// element offset of the padded scale grid (rows_pad x k) fits in 32 bits.
+bool quant_idx32(const g3::QuantParams& p) { return p.rows_pad * p.k < (int64_t(1) << 32); }
+
+template <int kInDtype>
+void* quant_kernel_fn(bool idx32) {
+  return idx32 ? reinterpret_cast<void*>(g3::nvfp4_quantize_kernel<kInDtype, uint32_t>)
+               : reinterpret_cast<void*>(g3::nvfp4_quantize_kernel<kInDtype, int64_t>);
+}
+
+void* quant_kernel_for(int32_t in_dtype, bool idx32) {
+  switch (in_dtype) {
+    case NVFP4_DTYPE_F16: return quant_kernel_fn<0>(idx32);
+    case NVFP4_DTYPE_BF16: return quant_kernel_fn<1>(idx32);
+    default: return quant_kernel_fn<2>(idx32);
+  }
+}
+
 // One full wave of the grid-stride quantiser: every SM holds as many blocks as fit, so no
 // partial second wave is left at the end.
-int quant_grid(DeviceCache* d, int32_t in_dtype, int64_t work) {
-  int& per_sm = d->quant_blocks[in_dtype];
+int quant_grid(DeviceCache* d, int32_t in_dtype, bool idx32, int64_t work) {
+  int& per_sm = d->quant_blocks[in_dtype][idx32 ? 0 : 1];
   if (per_sm == 0) {
     std::lock_guard<std::mutex> lock(g_mu);
     int n = 0;
-    cudaError_t e = cudaSuccess;
-    switch (in_dtype) {
-      case NVFP4_DTYPE_F16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, g3::nvfp4_quantize_kernel<0>, 256, 0); break;
-      case NVFP4_DTYPE_BF16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, g3::nvfp4_quantize_kernel<1>, 256, 0); break;
-      default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, g3::nvfp4_quantize_kernel<2>, 256, 0); break;
-    }
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_kernel_for(in_dtype, idx32), 256, 0);
     if (e != cudaSuccess || n < 1) {
       (void)cudaGetLastError();
       n = 4;
@@ -588,14 +602,11 @@ int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, flo
   p.sf_swz = static_cast<uint8_t*>(sf_swizzled);
   p.sf_lin = static_cast<uint8_t*>(sf_linear);
   p.gs_out = gs_out;
-  const int grid = quant_grid(d, in_dtype, p.rows_pad * p.cols_pad);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (in_dtype) {
-    case NVFP4_DTYPE_F16: g3::nvfp4_quantize_kernel<0><<<grid, 256, 0, s>>>(p); break;
-    case NVFP4_DTYPE_BF16: g3::nvfp4_quantize_kernel<1><<<grid, 256, 0, s>>>(p); break;
-    default: g3::nvfp4_quantize_kernel<2><<<grid, 256, 0, s>>>(p); break;
-  }
-  G3_CUDA(cudaGetLastError());
+  const bool idx32 = quant_idx32(p);
+  const int grid = quant_grid(d, in_dtype, idx32, p.rows_pad * p.cols_pad);
+  void* args[] = {&p};
+  G3_CUDA(cudaLaunchKernel(quant_kernel_for(in_dtype, idx32), dim3(static_cast<unsigned>(grid)), dim3(256), args, 0,
+                           static_cast<cudaStream_t>(stream)));
   return NVFP4_OK;
 }
 
@@ -675,7 +686,8 @@ int nvfp4_quantize_act(const void* x, int32_t in_dtype, int64_t rows, int64_t k,
   // For the few rows a weight-streaming GEMM follows (<= 128), at most one quantiser CTA per SM:
   // they become resident early (programmatic launch) and wait for the amax kernel, and each SM
   // must keep room for a GEMM CTA launched early the same way. Larger inputs get a full wave.
-  int qgrid = quant_grid(d, in_dtype, p.rows_pad * p.cols_pad);
+  const bool idx32 = quant_idx32(p);
+  int qgrid = quant_grid(d, in_dtype, idx32, p.rows_pad * p.cols_pad);
   if (rows <= 128 && qgrid > d->sm_count) qgrid = d->sm_count;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(qgrid), 1, 1);
@@ -688,10 +700,18 @@ int nvfp4_quantize_act(const void* x, int32_t in_dtype, int64_t rows, int64_t k,
   lc.numAttrs = 1;
   const uint32_t* cparts = ws;
   const int nparts = static_cast<int>(parts);
-  switch (in_dtype) {
-    case NVFP4_DTYPE_F16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<0>, p, cparts, nparts, gs_other, alpha_out)); break;
-    case NVFP4_DTYPE_BF16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<1>, p, cparts, nparts, gs_other, alpha_out)); break;
-    default: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<2>, p, cparts, nparts, gs_other, alpha_out)); break;
+  if (idx32) {
+    switch (in_dtype) {
+      case NVFP4_DTYPE_F16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<0, uint32_t>, p, cparts, nparts, gs_other, alpha_out)); break;
+      case NVFP4_DTYPE_BF16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<1, uint32_t>, p, cparts, nparts, gs_other, alpha_out)); break;
+      default: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<2, uint32_t>, p, cparts, nparts, gs_other, alpha_out)); break;
+    }
+  } else {
+    switch (in_dtype) {
+      case NVFP4_DTYPE_F16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<0, int64_t>, p, cparts, nparts, gs_other, alpha_out)); break;
+      case NVFP4_DTYPE_BF16: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<1, int64_t>, p, cparts, nparts, gs_other, alpha_out)); break;
+      default: G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_act_quantize_kernel<2, int64_t>, p, cparts, nparts, gs_other, alpha_out)); break;
+    }
   }
   return NVFP4_OK;
 }

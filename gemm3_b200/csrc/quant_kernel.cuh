@@ -208,36 +208,44 @@ __device__ __forceinline__ int64_t sf_swizzle_offset(int64_t row, int64_t col, i
   return ((row >> 7) * c4 + (col >> 2)) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + (col & 3);
 }
 
+// The raw bits of one 16-element block: 32 bytes of f16/bf16 or 64 bytes of f32.
 template <int kInDtype>  // 0 = f16, 1 = bf16, 2 = f32
-__device__ __forceinline__ void load16(const void* base, int64_t elem, float (&v)[16]) {
-  if constexpr (kInDtype == 2) {
-    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + elem);
+struct RawBlock {
+  uint4 w[kInDtype == 2 ? 4 : 2];
+};
+
+template <int kInDtype>
+__device__ __forceinline__ void load_raw(const void* base, int64_t elem, RawBlock<kInDtype>& rb) {
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + elem * (kInDtype == 2 ? 4 : 2));
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 f = __ldg(p + i);
-      v[4 * i] = f.x;
-      v[4 * i + 1] = f.y;
-      v[4 * i + 2] = f.z;
-      v[4 * i + 3] = f.w;
-    }
-  } else {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + elem);
+  for (int i = 0; i < (kInDtype == 2 ? 4 : 2); ++i) rb.w[i] = __ldg(p + i);
+}
+
+template <int kInDtype>
+__device__ __forceinline__ void unpack_raw(const RawBlock<kInDtype>& rb, float (&v)[16]) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint4 w = __ldg(p + i);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  for (int i = 0; i < (kInDtype == 2 ? 4 : 2); ++i) {
+    const uint32_t ws[4] = {rb.w[i].x, rb.w[i].y, rb.w[i].z, rb.w[i].w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if constexpr (kInDtype == 1) {
-          v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
-          v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
-        } else {
-          v[8 * i + 2 * j] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[j] & 0xFFFFu)));
-          v[8 * i + 2 * j + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[j] >> 16)));
-        }
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (kInDtype == 2) {
+        v[4 * i + j] = __uint_as_float(ws[j]);
+      } else if constexpr (kInDtype == 1) {
+        v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+      } else {
+        v[8 * i + 2 * j] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[j] & 0xFFFFu)));
+        v[8 * i + 2 * j + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[j] >> 16)));
       }
     }
   }
+}
+
+template <int kInDtype>
+__device__ __forceinline__ void load16(const void* base, int64_t elem, float (&v)[16]) {
+  RawBlock<kInDtype> rb;
+  load_raw<kInDtype>(base, elem, rb);
+  unpack_raw<kInDtype>(rb, v);
 }
 
 struct QuantParams {
@@ -265,13 +273,14 @@ __device__ __forceinline__ float resolve_global_scale(const QuantParams& p) {
 
 // One 16-element block (r, c) of the padded scale grid: codes, linear and swizzled scale. Blocks
 // outside the logical shape write a zero scale into the swizzled padding only.
-template <int kInDtype>
-__device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, int64_t r, int64_t c, int64_t c4) {
+template <int kInDtype, typename Idx>
+__device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, Idx r, Idx c, Idx c4, Idx elem,
+                                               bool inside, const RawBlock<kInDtype>& rb) {
   const float inv6 = 0.166666672f;  // fl(1/6): what torch on CUDA multiplies by for "/ 6.0"
   uint32_t sf = 0;
-  if (r < p.rows && c < p.cols) {
+  if (inside) {
     float v[16];
-    load16<kInDtype>(p.x, r * p.k + c * 16, v);
+    unpack_raw<kInDtype>(rb, v);
     const float2 gs2 = make_float2(gs, gs);
 #pragma unroll
     for (int i = 0; i < 16; i += 2) {
@@ -302,32 +311,48 @@ __device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, i
       codes = mn >= 0x1p-100f ? make_uint2(e2m1_pack8_signed(v, denom, rd), e2m1_pack8_signed(v + 8, denom, rd))
                               : e2m1_pack16(v, denom, rd);
     }
-    *reinterpret_cast<uint2*>(p.packed + r * (p.k >> 1) + c * 8) = codes;
-    if (p.sf_lin != nullptr) p.sf_lin[r * p.cols + c] = static_cast<uint8_t>(sf);
+    // elem = r * k + 16 c: the block's codes start at byte elem / 2, its linear scale at elem / 16
+    *reinterpret_cast<uint2*>(p.packed + (elem >> 1)) = codes;
+    if (p.sf_lin != nullptr) p.sf_lin[elem >> 4] = static_cast<uint8_t>(sf);
   }
-  p.sf_swz[sf_swizzle_offset(r, c, c4)] = static_cast<uint8_t>(sf);
+  p.sf_swz[((r >> 7) * c4 + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3)] = static_cast<uint8_t>(sf);
 }
 
-template <int kInDtype>
-__global__ void __launch_bounds__(256) nvfp4_quantize_kernel(const QuantParams p) {
-  const float gs = resolve_global_scale(p);
-  if (p.gs_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.gs_out = gs;
-  const int64_t total = p.rows_pad * p.cols_pad;
-  const int64_t c4 = p.cols_pad >> 2;
-  // Block (r, c) of the padded scale grid, advanced by the grid stride without dividing.
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t dr = stride / p.cols_pad, dc = stride - dr * p.cols_pad;
-  int64_t r = b0 / p.cols_pad, c = b0 - r * p.cols_pad;
-  for (int64_t b = b0; b < total; b += stride) {
-    quantize_block<kInDtype>(p, gs, r, c, c4);
+// The grid-stride walk over the blocks (r, c) of the padded scale grid, advanced by the stride
+// without dividing. Idx is uint32_t when every element offset of the padded grid fits in 32 bits
+// (the host checks rows_pad * k < 2^32), which keeps the per-block index arithmetic to single
+// instructions; int64_t otherwise. (Loading the next block before converting the current one
+// was measured: no gain for 16-bit inputs, 14 more registers.)
+template <int kInDtype, typename Idx>
+__device__ __forceinline__ void quantize_grid_stride(const QuantParams& p, float gs) {
+  const Idx rows = static_cast<Idx>(p.rows), cols = static_cast<Idx>(p.cols), k = static_cast<Idx>(p.k);
+  const Idx cols_pad = static_cast<Idx>(p.cols_pad);
+  const Idx total = static_cast<Idx>(p.rows_pad) * cols_pad;
+  const Idx c4 = cols_pad >> 2;
+  const Idx stride = static_cast<Idx>(gridDim.x) * blockDim.x;
+  const Idx b0 = static_cast<Idx>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const Idx dr = stride / cols_pad, dc = stride - dr * cols_pad;
+  Idx r = b0 / cols_pad, c = b0 - r * cols_pad;
+  for (Idx b = b0; b < total; b += stride) {
+    const bool inside = r < rows && c < cols;
+    const Idx elem = r * k + c * 16;
+    RawBlock<kInDtype> rb;
+    if (inside) load_raw<kInDtype>(p.x, static_cast<int64_t>(elem), rb);
+    quantize_block<kInDtype, Idx>(p, gs, r, c, c4, elem, inside, rb);
     c += dc;
     r += dr;
-    if (c >= p.cols_pad) {
-      c -= p.cols_pad;
+    if (c >= cols_pad) {
+      c -= cols_pad;
       ++r;
     }
   }
+}
+
+template <int kInDtype, typename Idx>
+__global__ void __launch_bounds__(256) nvfp4_quantize_kernel(const QuantParams p) {
+  const float gs = resolve_global_scale(p);
+  if (p.gs_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.gs_out = gs;
+  quantize_grid_stride<kInDtype, Idx>(p, gs);
 }
 
 // Activation quantiser for an LLM projection call, as two launches chained by programmatic
@@ -368,7 +393,7 @@ __global__ void __launch_bounds__(kActThreads) nvfp4_act_amax_kernel(const void*
   }
 }
 
-template <int kInDtype>
+template <int kInDtype, typename Idx>
 __global__ void __launch_bounds__(kActThreads)
     nvfp4_act_quantize_kernel(const QuantParams p, const uint32_t* parts, int n_parts, const float* gs_other,
                               float* alpha_out) {
@@ -390,21 +415,7 @@ __global__ void __launch_bounds__(kActThreads)
     if (p.gs_out != nullptr) *p.gs_out = gs;
     if (alpha_out != nullptr) *alpha_out = __frcp_rn(__fmul_rn(gs, *gs_other));
   }
-  const int64_t total = p.rows_pad * p.cols_pad;
-  const int64_t c4 = p.cols_pad >> 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t dr = stride / p.cols_pad, dc = stride - dr * p.cols_pad;
-  int64_t r = b0 / p.cols_pad, c = b0 - r * p.cols_pad;
-  for (int64_t b = b0; b < total; b += stride) {
-    quantize_block<kInDtype>(p, gs, r, c, c4);
-    c += dc;
-    r += dr;
-    if (c >= p.cols_pad) {
-      c -= p.cols_pad;
-      ++r;
-    }
-  }
+  quantize_grid_stride<kInDtype, Idx>(p, gs);
 }
 
 struct DequantParams {

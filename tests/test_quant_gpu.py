@@ -119,6 +119,27 @@ def test_quantize_near_rounding_boundaries(cuda_ext):
     np.testing.assert_array_equal(sf_swz.cpu().numpy(), want[1])
 
 
+def test_quantize_2pow32_elements_matches_row_slices(cuda_ext):
+    """2^32 elements (8 GiB of BF16): the kernel walks the grid with 64-bit indices there, and
+    with 32-bit ones for anything smaller. Row blocks at both ends (the last ones past 2^31 and
+    near 2^32 elements) quantised on their own must give the same bytes, in all three outputs."""
+    rows, k = 1 << 18, 1 << 14
+    x = torch.empty(rows, k, device="cuda", dtype=torch.bfloat16)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for r0 in range(0, rows, 16384):
+        x[r0:r0 + 16384] = torch.randn(16384, k, device="cuda", generator=g).to(torch.bfloat16)
+    gs = torch.tensor([2688.0 / 5.5], device="cuda")
+    packed, sf_swz, sf_lin = cuda_ext.quantize_nvfp4(x, gs)
+    chunk = 128 * (k // 64) * 4  # swizzled scale bytes of one 128-row block
+    for r0 in (0, (1 << 17) + 128, rows - 256):
+        p2, s2, l2 = cuda_ext.quantize_nvfp4(x[r0:r0 + 256], gs)
+        assert torch.equal(packed[r0:r0 + 256], p2)
+        assert torch.equal(sf_lin[r0:r0 + 256], l2)
+        assert torch.equal(sf_swz[r0 // 128 * chunk:(r0 // 128 + 2) * chunk], s2)
+    del x, packed, sf_swz, sf_lin
+    torch.cuda.empty_cache()
+
+
 def test_amax_odd_sizes_and_nan(cuda_ext):
     for n in (1, 15, 16, 17, 1000003):
         x = torch.randn(n, device="cuda")
