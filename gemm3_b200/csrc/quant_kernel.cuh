@@ -39,22 +39,6 @@
 
 namespace g3 {
 
-// FP32 -> E4M3 (fn variant: bias 7, max 448, 0x7F/0xFF = NaN, no infinities), round to nearest
-// even, non-saturating: anything that rounds above 448 becomes NaN.
-__device__ __forceinline__ uint32_t f32_to_e4m3_rn(float f) {
-  const uint32_t u = __float_as_uint(f);
-  const uint32_t sign = (u >> 24) & 0x80u;
-  const uint32_t a = u & 0x7FFFFFFFu;
-  if (a > 0x43E80000u) return sign | 0x7Fu;  // NaN, Inf, or |f| > 464 (rounds past 448)
-  if (a >= 0x3C800000u) {                    // |f| >= 2^-6: normal E4M3
-    const uint32_t r = (a + 0x7FFFFu + ((a >> 20) & 1u)) >> 20;  // keep 3 mantissa bits, RNE
-    return sign | (r - (120u << 3));                             // rebias exponent 127 -> 7
-  }
-  // Subnormal E4M3: multiples of 2^-9. f * 512 is exact; rintf rounds half to even.
-  const uint32_t q = static_cast<uint32_t>(rintf(__uint_as_float(a) * 512.0f));
-  return sign | q;  // q == 8 is the smallest normal (0x08), which is also correct
-}
-
 __device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
   const uint32_t sign = (b & 0x80u) << 24;
   const uint32_t e = (b >> 3) & 0xFu;
@@ -62,6 +46,24 @@ __device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
   if (e == 0xFu && m == 7u) return __uint_as_float(sign | 0x7FC00000u);
   if (e == 0) return __uint_as_float(sign | __float_as_uint(static_cast<float>(m) * 0.001953125f));
   return __uint_as_float(sign | ((e + 120u) << 23) | (m << 20));
+}
+
+// FP32 -> E4M3 (fn variant: bias 7, max 448, 0x7F/0xFF = NaN, no infinities) as torch's
+// float8_e4m3fn cast does it: round to nearest even, non-saturating. cvt.rn.satfinite.e4m3x2.f32
+// rounds the same way but saturates, so anything above 464 (the midpoint between 448 and the
+// first value past it, which ties down to 448) and NaN are mapped to 0x7F by one compare; s is
+// never negative here. E4M3 values are exact in FP16, so the decode goes through
+// cvt.rn.f16x2.e4m3x2 (e4m3_to_f32 below is the bit-level decode the dequantiser uses).
+__device__ __forceinline__ uint32_t e4m3_encode_nonneg(float s) {
+  uint16_t h;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(0.0f), "f"(s));
+  return s <= 464.0f ? static_cast<uint32_t>(h & 0xFFu) : 0x7Fu;
+}
+
+__device__ __forceinline__ float e4m3_decode(uint32_t b) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(b)));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
 }
 
 __device__ __constant__ float kE2M1Table[9] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f, 6.0f};
@@ -289,7 +291,7 @@ __device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, I
       v[i + 1] = xb.y;
     }
     // amax is NaN if any element is NaN and Inf if one is infinite: the reference's scale is NaN
-    // either way (NaN amax, or Inf / 6 overflowing E4M3), and f32_to_e4m3_rn maps both to 0x7F.
+    // either way (NaN amax, or Inf / 6 overflowing E4M3), and e4m3_encode_nonneg maps both to 0x7F.
     // mn, the smallest magnitude, picks the arithmetic below.
     float amax = max3_nan(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
     float mn = min3(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
@@ -301,8 +303,8 @@ __device__ __forceinline__ void quantize_block(const QuantParams& p, float gs, I
     amax = max_nan(amax, fabsf(v[15]));
     mn = fminf(mn, fabsf(v[15]));
     const float s = p.div_mode == 0 ? __fmul_rn(amax, inv6) : __fdiv_rn(amax, 6.0f);
-    sf = f32_to_e4m3_rn(s);
-    const float denom = e4m3_to_f32(sf);
+    sf = e4m3_encode_nonneg(s);
+    const float denom = e4m3_decode(sf);
     // else q = 0 for every element: code 0 (a NaN scale included). Blocks holding a zero or a
     // magnitude below 2^-100 take the general path, which decides signs without the quotient.
     uint2 codes = make_uint2(0u, 0u);

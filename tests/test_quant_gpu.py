@@ -119,6 +119,30 @@ def test_quantize_near_rounding_boundaries(cuda_ext):
     np.testing.assert_array_equal(sf_swz.cpu().numpy(), want[1])
 
 
+def test_scale_encoding_sweep(cuda_ext):
+    """Block scales at, and one ulp either side of, every E4M3 rounding midpoint (including 464,
+    above which the reference's scale is NaN) and at every E4M3 value, through both roundings of
+    '/ 6': the exact division (CPU tensors) and the multiply by fl(1/6) (CUDA tensors)."""
+    vals = torch.arange(0x7F, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    vals = np.concatenate([vals, [480.0]]).astype(np.float32)  # 480: one step past 448
+    s = []
+    for a, b in zip(vals[:-1], vals[1:]):
+        m = np.float32((np.float64(a) + np.float64(b)) / 2)
+        s += [np.nextafter(m, np.float32(0)), m, np.nextafter(m, np.float32(1e9)), a]
+    s = np.array(s, np.float32)
+    amax = (s.astype(np.float64) * 6).astype(np.float32)  # exactly 6 m for the midpoints
+    blocks = np.tile((amax * np.float32(0.5))[:, None], (1, 16)).astype(np.float32)
+    blocks[:, 0] = amax
+    blocks = np.concatenate([blocks, np.zeros(((-len(blocks)) % 4, 16), np.float32)])
+    x = blocks.reshape(-1, 64)
+    for xt, div_mode in ((torch.from_numpy(x), 1), (torch.from_numpy(x).cuda(), 0)):
+        packed, sf_swz, sf_lin = cuda_ext.quantize_nvfp4(xt, 1.0)
+        want = oracle.quantize(x, 1.0, div_mode=div_mode)
+        np.testing.assert_array_equal(sf_lin.cpu().numpy(), want[2])
+        np.testing.assert_array_equal(sf_swz.cpu().numpy(), want[1])
+        np.testing.assert_array_equal(packed.cpu().numpy(), want[0])
+
+
 def test_quantize_2pow32_elements_matches_row_slices(cuda_ext):
     """2^32 elements (8 GiB of BF16): the kernel walks the grid with 64-bit indices there, and
     with 32-bit ones for anything smaller. Row blocks at both ends (the last ones past 2^31 and
