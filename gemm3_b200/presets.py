@@ -17,7 +17,7 @@ Measured on B200 (python -m gemm3_b200.tune, BF16 out; outputs bit-identical acr
   - the CTA-pair tile beats the one-CTA tile at every size (8192^3: 215 against 371 us; the
     one-CTA tile reads 42 % more from L2);
   - at 16384^3 the fast_swz=2 band with cluster (8, 2) is 16 % faster than plain raster, raster
-    along M, or bands of 4 or 8 (1579 against 1749-1890 us): it keeps the B tiles in sweep
+    along M, or fast_swz 1, 4 or 8 (1579 against 1749-1890 us): it keeps the B tiles in sweep
     resident in L2; A/SFA evict_last adds 1 %;
   - at 8192^3 and 4096^3 (operands resident in L2) raster and L2 attributes change the time by at
     most one 2-us timer step.
