@@ -41,8 +41,8 @@ struct DeviceCache {
   bool gemm_attr_set = false;
   bool stream_attr_set = false;
   int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
-  // co-resident 256-thread quantiser blocks per SM, per input dtype and index width (32 / 64 bits)
-  int quant_blocks[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+  // co-resident 256-thread quantiser blocks per SM, per input dtype and QuantKind
+  int quant_blocks[3][3] = {{0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
 };
 DeviceCache g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -162,32 +162,49 @@ int grid_for(int64_t work, int sm_count, int threads = 256) {
   return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
-// The quantiser instantiation for an input dtype and index width: 32-bit indices whenever every
-// element offset of the padded scale grid (rows_pad x k) fits in 32 bits.
+// The quantiser kernels: one block per thread with 32-bit indices whenever every element offset
+// of the padded scale grid (rows_pad x k) fits in 32 bits, else with 64-bit ones; and, for 16-bit
+// inputs whose rows hold whole pairs of blocks and whose outputs are aligned for the wider
+// stores, two blocks per thread.
+enum QuantKind { kQuantIdx32 = 0, kQuantIdx64 = 1, kQuantPair = 2 };
+
 bool quant_idx32(const g3::QuantParams& p) { return p.rows_pad * p.k < (int64_t(1) << 32); }
 
-template <int kInDtype>
-void* quant_kernel_fn(bool idx32) {
-  return idx32 ? reinterpret_cast<void*>(g3::nvfp4_quantize_kernel<kInDtype, uint32_t>)
-               : reinterpret_cast<void*>(g3::nvfp4_quantize_kernel<kInDtype, int64_t>);
+QuantKind quant_kind(const g3::QuantParams& p, int32_t in_dtype) {
+  if (!quant_idx32(p)) return kQuantIdx64;
+  if (in_dtype != NVFP4_DTYPE_F32 && p.k % 32 == 0 && aligned(p.packed, 16) && aligned(p.sf_swz, 2) &&
+      (p.sf_lin == nullptr || aligned(p.sf_lin, 2)))
+    return kQuantPair;
+  return kQuantIdx32;
 }
 
-void* quant_kernel_for(int32_t in_dtype, bool idx32) {
+template <int kInDtype>
+void* quant_kernel_fn(QuantKind kind) {
+  switch (kind) {
+    case kQuantIdx32: return reinterpret_cast<void*>(g3::nvfp4_quantize_kernel<kInDtype, uint32_t>);
+    case kQuantIdx64: return reinterpret_cast<void*>(g3::nvfp4_quantize_kernel<kInDtype, int64_t>);
+    default:
+      if constexpr (kInDtype != 2) return reinterpret_cast<void*>(g3::nvfp4_quantize_pair_kernel<kInDtype>);
+      return nullptr;  // not selected for f32 (quant_kind)
+  }
+}
+
+void* quant_kernel_for(int32_t in_dtype, QuantKind kind) {
   switch (in_dtype) {
-    case NVFP4_DTYPE_F16: return quant_kernel_fn<0>(idx32);
-    case NVFP4_DTYPE_BF16: return quant_kernel_fn<1>(idx32);
-    default: return quant_kernel_fn<2>(idx32);
+    case NVFP4_DTYPE_F16: return quant_kernel_fn<0>(kind);
+    case NVFP4_DTYPE_BF16: return quant_kernel_fn<1>(kind);
+    default: return quant_kernel_fn<2>(kind);
   }
 }
 
 // One full wave of the grid-stride quantiser: every SM holds as many blocks as fit, so no
 // partial second wave is left at the end.
-int quant_grid(DeviceCache* d, int32_t in_dtype, bool idx32, int64_t work) {
-  int& per_sm = d->quant_blocks[in_dtype][idx32 ? 0 : 1];
+int quant_grid(DeviceCache* d, int32_t in_dtype, QuantKind kind, int64_t work) {
+  int& per_sm = d->quant_blocks[in_dtype][kind];
   if (per_sm == 0) {
     std::lock_guard<std::mutex> lock(g_mu);
     int n = 0;
-    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_kernel_for(in_dtype, idx32), 256, 0);
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_kernel_for(in_dtype, kind), 256, 0);
     if (e != cudaSuccess || n < 1) {
       (void)cudaGetLastError();
       n = 4;
@@ -602,10 +619,11 @@ int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, flo
   p.sf_swz = static_cast<uint8_t*>(sf_swizzled);
   p.sf_lin = static_cast<uint8_t*>(sf_linear);
   p.gs_out = gs_out;
-  const bool idx32 = quant_idx32(p);
-  const int grid = quant_grid(d, in_dtype, idx32, p.rows_pad * p.cols_pad);
+  const QuantKind kind = quant_kind(p, in_dtype);
+  const int64_t work = kind == kQuantPair ? p.rows_pad * (p.cols_pad / 2) : p.rows_pad * p.cols_pad;
+  const int grid = quant_grid(d, in_dtype, kind, work);
   void* args[] = {&p};
-  G3_CUDA(cudaLaunchKernel(quant_kernel_for(in_dtype, idx32), dim3(static_cast<unsigned>(grid)), dim3(256), args, 0,
+  G3_CUDA(cudaLaunchKernel(quant_kernel_for(in_dtype, kind), dim3(static_cast<unsigned>(grid)), dim3(256), args, 0,
                            static_cast<cudaStream_t>(stream)));
   return NVFP4_OK;
 }
@@ -687,7 +705,7 @@ int nvfp4_quantize_act(const void* x, int32_t in_dtype, int64_t rows, int64_t k,
   // they become resident early (programmatic launch) and wait for the amax kernel, and each SM
   // must keep room for a GEMM CTA launched early the same way. Larger inputs get a full wave.
   const bool idx32 = quant_idx32(p);
-  int qgrid = quant_grid(d, in_dtype, idx32, p.rows_pad * p.cols_pad);
+  int qgrid = quant_grid(d, in_dtype, idx32 ? kQuantIdx32 : kQuantIdx64, p.rows_pad * p.cols_pad);
   if (rows <= 128 && qgrid > d->sm_count) qgrid = d->sm_count;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(qgrid), 1, 1);

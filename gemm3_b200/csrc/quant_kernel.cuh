@@ -389,6 +389,50 @@ __global__ void __launch_bounds__(256, kInDtype == 2 ? 4 : (sizeof(Idx) == 4 ? 8
   quantize_grid_stride<kInDtype, Idx>(p, gs);
 }
 
+// Two consecutive blocks of a row per thread, for 16-bit inputs: 64 bytes loaded per thread (as
+// one f32 block), one 16-byte code store and one 16-bit store of the two scales in each layout.
+// The host takes it when k % 32 == 0 (so both blocks of a pair are inside the row or both in the
+// padding), rows_pad * k < 2^32, the packed codes are 16-byte and both scale arrays 2-byte
+// aligned. The per-element arithmetic is nvfp4_quantize_kernel's.
+template <int kInDtype>
+__global__ void __launch_bounds__(256) nvfp4_quantize_pair_kernel(const QuantParams p) {
+  static_assert(kInDtype != 2, "f32 inputs use nvfp4_quantize_kernel");
+  const float gs = resolve_global_scale(p);
+  if (p.gs_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.gs_out = gs;
+  const uint32_t rows = static_cast<uint32_t>(p.rows), cols = static_cast<uint32_t>(p.cols);
+  const uint32_t k = static_cast<uint32_t>(p.k);
+  const uint32_t c2 = static_cast<uint32_t>(p.cols_pad >> 1);  // block pairs per padded row
+  const uint32_t c4 = static_cast<uint32_t>(p.cols_pad >> 2);
+  const uint32_t total = static_cast<uint32_t>(p.rows_pad) * c2;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint32_t b0 = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t dr = stride / c2, dq = stride - dr * c2;
+  uint32_t r = b0 / c2, q = b0 - r * c2;
+  for (uint32_t b = b0; b < total; b += stride) {
+    const uint32_t c = 2 * q;
+    uint32_t sf2 = 0;
+    if (r < rows && c < cols) {
+      const uint32_t elem = r * k + c * 16;
+      RawBlock<kInDtype> rb0, rb1;
+      load_raw<kInDtype>(p.x, static_cast<int64_t>(elem), rb0);
+      load_raw<kInDtype>(p.x, static_cast<int64_t>(elem + 16), rb1);
+      uint2 w0, w1;
+      sf2 = quantize_values<kInDtype>(rb0, gs, p.div_mode, w0);
+      sf2 |= quantize_values<kInDtype>(rb1, gs, p.div_mode, w1) << 8;
+      *reinterpret_cast<uint4*>(p.packed + (elem >> 1)) = make_uint4(w0.x, w0.y, w1.x, w1.y);
+      if (p.sf_lin != nullptr) *reinterpret_cast<uint16_t*>(p.sf_lin + (elem >> 4)) = static_cast<uint16_t>(sf2);
+    }
+    *reinterpret_cast<uint16_t*>(p.sf_swz + ((r >> 7) * c4 + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 +
+                                 (c & 3)) = static_cast<uint16_t>(sf2);
+    q += dq;
+    r += dr;
+    if (q >= c2) {
+      q -= c2;
+      ++r;
+    }
+  }
+}
+
 // Activation quantiser for an LLM projection call, as two launches chained by programmatic
 // dependent launch (each lets the next kernel in the stream start as its first instruction):
 //   nvfp4_act_amax_kernel      every CTA writes the max |x| bits of its grid-stride share to
