@@ -143,6 +143,39 @@ def test_scale_encoding_sweep(cuda_ext):
         np.testing.assert_array_equal(packed.cpu().numpy(), want[0])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_quantize_output_alignment_paths_agree(cuda_ext, dtype):
+    """16-bit inputs with k % 32 == 0 go to the two-blocks-per-thread kernel when the codes are
+    16-byte and the scale arrays 2-byte aligned, else to the one-block kernel. Outputs written at
+    odd offsets (through the C ABI) must hold the same bytes as aligned ones."""
+    from gemm3_b200 import _lib
+    from gemm3_b200.quant import sf_swizzled_size
+
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    rows, k = 300, 2048
+    x = (torch.randn(rows, k, device=dev, generator=g) * 4.0).to(dtype)
+    code = _lib.DTYPE_BF16 if dtype == torch.bfloat16 else _lib.DTYPE_F16
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    nsw = sf_swizzled_size(rows, k)
+    outs = []
+    for off_p, off_s in ((0, 0), (8, 1)):  # aligned; codes 8-byte and scales 1-byte aligned only
+        packed = torch.zeros(rows * k // 2 + 16, dtype=torch.uint8, device=dev)
+        sf_swz = torch.zeros(nsw + 2, dtype=torch.uint8, device=dev)
+        sf_lin = torch.zeros(rows * k // 16 + 2, dtype=torch.uint8, device=dev)
+        rc = L.nvfp4_quantize(x.data_ptr(), code, rows, k, 1.7, None, 0, 0, packed.data_ptr() + off_p,
+                              sf_swz.data_ptr() + off_s, sf_lin.data_ptr() + off_s, None, stream)
+        assert rc == _lib.OK, L.nvfp4_strerror(rc)
+        outs.append((packed[off_p:off_p + rows * k // 2], sf_swz[off_s:off_s + nsw], sf_lin[off_s:off_s + rows * k // 16]))
+    torch.cuda.synchronize()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    want = oracle.quantize(x.float().cpu().numpy(), 1.7, div_mode=0)
+    np.testing.assert_array_equal(outs[0][0].cpu().numpy().reshape(rows, k // 2), want[0])
+    np.testing.assert_array_equal(outs[0][1].cpu().numpy(), want[1])
+
+
 def test_quantize_2pow32_elements_matches_row_slices(cuda_ext):
     """2^32 elements (8 GiB of BF16): the kernel walks the grid with 64-bit indices there, and
     with 32-bit ones for anything smaller. Row blocks at both ends (the last ones past 2^31 and
