@@ -20,15 +20,19 @@
 // (checked exhaustively on the CPU); exponents only shift the result while no intermediate
 // leaves the normal range, which holds for |xb| >= 2^-100. Below that |q| < 2^-91, so the
 // magnitude code is 0 however q rounds, and the sign bit is decided from xb and the scale
-// directly (e2m1_pack16).
+// directly (e2m1_pack16). Blocks whose every |xb| is at least 2^-100 (the common case) take
+// e2m1_pack8_signed, where the conversions of the signed quotient set the sign bits.
 //
 // The codes themselves come from the hardware E2M1 conversion (round-to-nearest-even); the
 // reference's tie rule is applied exactly by a check that sends only elements next to a rounding
-// tie to its thresholds (e2m1_pack8).
+// tie to its thresholds. The block scale goes through the hardware E4M3 conversion, with the
+// reference's overflow to NaN applied by one compare (e4m3_encode_nonneg).
 //
-// One thread owns one 16-element scale block. Consecutive threads own consecutive blocks of
-// the row-major input, so loads (32 or 64 bytes per thread), code stores (8 bytes) and linear
-// scale stores are coalesced; the swizzled scale byte goes to its 128x4-tile position.
+// For 16-bit inputs whose rows hold whole pairs of blocks one thread owns two neighbouring
+// 16-element blocks (nvfp4_quantize_pair_kernel); otherwise one (nvfp4_quantize_kernel).
+// Consecutive threads own consecutive blocks of the row-major input, so loads (32 or 64 bytes
+// per thread), code stores (8 or 16 bytes) and linear scale stores are coalesced; the swizzled
+// scales go to their 128x4-tile position.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
