@@ -136,7 +136,9 @@ int nvfp4_ipc_close(void* ptr, int64_t offset);
  *   0: amax * fl(1/6) (PyTorch on CUDA divides by a host scalar through its reciprocal);
  *   1: correctly rounded amax / 6 (PyTorch on CPU).
  * Outputs: packed [rows, K/2]; sf_swizzled (padding written as zeros); sf_linear [rows, K/16]
- * (may be NULL). Requires K % 16 == 0.
+ * (may be NULL). Requires K % 16 == 0 and packed 8-byte aligned. For F16/BF16 input with
+ * K % 32 == 0, packed 16-byte aligned and both scale arrays 2-byte aligned, one thread
+ * converts two neighbouring 16-element blocks (wider loads and stores; the same bytes).
  */
 int nvfp4_quantize(const void* x, int32_t in_dtype, int64_t rows, int64_t k, float global_scale,
                    const float* gs_dev, int32_t gs_mode, int32_t div_mode, void* packed,
