@@ -53,6 +53,7 @@ def parse():
     p.add_argument("--allgather", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-vendor", action="store_true", help="skip the cuBLASLt timing on the same workload")
+    p.add_argument("--no-quantiser", action="store_true", help="skip the timing of the operand quantiser")
     p.add_argument("--e2e-steps", type=int, default=12)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-rows", type=int, default=128)
@@ -422,6 +423,10 @@ def run_ours(args):
     if world == 1 and not args.no_vendor:
         vendor = time_cublaslt(sets, out_dtype, dev, M, N, K)
 
+    quantiser = None
+    if world == 1 and not args.no_quantiser:
+        quantiser = time_quantiser(M, K, dev)
+
     e2e = None
     if not args.no_e2e:
         e2e = time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world)
@@ -475,6 +480,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": e2e,
         "vendor": vendor,
+        "quantiser": quantiser,
     }
     if allgather is not None:
         line["allgather"] = allgather
@@ -484,6 +490,63 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def time_quantiser(rows, k, dev):
+    """The quantiser that prepares the bench's operands, on this GPU: rows x k seeded N(0,1) BF16
+    -> NVFP4 with a device-side global scale 2688 / amax (codes, swizzled and linear scales). Three
+    rotating inputs, together larger than L2, 30 calls per CUDA-graph replay, median of five
+    replays after one warm replay; the call allocates its outputs from the graph's pool.
+    Algorithmic bytes per element: 2 read + 0.5 codes + 1/16 swizzled + 1/16 linear scale."""
+    import torch
+
+    import gemm3_b200 as g3
+
+    g = torch.Generator(device=dev).manual_seed(99)
+    xs = [torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
+    gss = [torch.full((1,), 2688.0, device=dev) / g3.tensor_amax(x) for x in xs]
+    per = 30
+
+    def calls():
+        for i in range(per):
+            g3.quantize_nvfp4(xs[i % 3], gss[i % 3])
+
+    calls()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            calls()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream(dev)
+    samples = []
+    for _ in range(6):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        gr.replay()
+        e1.record(cur)
+        e1.synchronize()
+        samples.append(e0.elapsed_time(e1) * 1e3 / per)
+    del gr, xs
+    us = statistics.median(samples[1:])
+    nbytes = rows * k * (2 + 0.5 + 1 / 16 + 1 / 16)
+    _, hbm, src = peaks()
+    return {
+        "kernel": "nvfp4_quantize_pair_kernel (BF16 in)" if k % 32 == 0 else "nvfp4_quantize_kernel (BF16 in)",
+        "shape": [rows, k],
+        "us": us,
+        "bound": "hbm",
+        "achieved": nbytes / (us * 1e-6) / 1e9,
+        "peak": hbm,
+        "unit": "GB/s",
+        "frac": nbytes / (us * 1e-6) / 1e9 / hbm,
+        "algorithmic_bytes": nbytes,
+        "peak_source": "hbm_gbs of MEASURED_PEAKS.json" if src == "measured" else "fallback 6650 GB/s",
+        "timing": "CUDA events around CUDA-graph replays of 30 back-to-back calls over 3 rotating inputs > L2",
+    }
 
 
 def time_allgather(c, world, dev):
