@@ -1,4 +1,4 @@
-"""CPU: the two arithmetic identities the GPU quantiser relies on, pinned against the reference
+"""CPU: the arithmetic identities the GPU quantiser relies on, pinned against the reference
 restatement (oracle/) and against IEEE division.
 
 1. The E2M1 code of q (quant.py:15-28) is the number of thresholds T1..T7 that |q| reaches.
@@ -6,6 +6,8 @@ restatement (oracle/) and against IEEE division.
    checked on windows around each of them and on a strided sweep of [0, 6].
 2. Markstein's correction with a correctly rounded reciprocal reproduces x / d exactly for every
    E4M3 divisor significand (an exhaustive C check).
+3. The block scale through a saturating round-to-nearest-even E4M3 conversion, with values above
+   464 (and NaN) sent to 0x7F by one compare, equals the reference's non-saturating encode.
 """
 
 import os
@@ -107,3 +109,42 @@ def test_rne_window_fast_path_matches_reference_rounding():
     fast = lo == hi
     np.testing.assert_array_equal(lo[fast], oracle_codes(bits)[fast])
     assert fast.mean() > 0.99  # the exact fallback is rare
+
+
+def _rne_e4m3_saturating(s):
+    """Round-to-nearest-even onto the finite E4M3 (fn) values, clamped to 448: what a
+    saturating conversion (cvt.rn.satfinite.e4m3x2.f32) gives for finite non-negative s."""
+    import torch
+
+    vals = torch.arange(0x7F, dtype=torch.uint8).view(torch.float8_e4m3fn).double().numpy()  # 0x00-0x7E
+    s = np.asarray(s, dtype=np.float64)
+    hi = np.clip(np.searchsorted(vals, s, side="left"), 1, len(vals) - 1)
+    lo = hi - 1
+    d_lo, d_hi = s - vals[lo], vals[hi] - s
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo)
+    code = np.where(s >= vals[-1], len(vals) - 1, code)
+    return code.astype(np.uint8)
+
+
+def test_saturating_e4m3_with_overflow_compare_matches_reference_encode():
+    """The kernel encodes the block scale s = amax / 6 (s >= 0 or NaN) as
+    (s <= 464 ? saturating RNE(s) : 0x7F). Checked against the oracle's non-saturating,
+    round-to-nearest-even encode (torch's float8_e4m3fn cast): within 64 ulps of every E4M3 value
+    and of every midpoint between neighbours (including 464, between 448 and the first value past
+    it), on a strided sweep of [0, 1024], and on Inf and NaN."""
+    import torch
+
+    vals = torch.arange(0x7F, dtype=torch.uint8).view(torch.float8_e4m3fn).double().numpy()
+    points = np.concatenate([vals, (vals[:-1] + vals[1:]) / 2, [464.0, 480.0]]).astype(np.float32)
+    windows = [np.arange(max(int(b) - 64, 0), int(b) + 64, dtype=np.uint32).view(np.float32)
+               for b in points.view(np.uint32)]
+    sweep = np.arange(0, int(np.float32(1024.0).view(np.uint32)), 1009, dtype=np.uint32).view(np.float32)
+    s = np.concatenate([sweep, *windows]).astype(np.float32)
+    want = oracle.e4m3_encode(s)
+    got = np.where(s <= np.float32(464.0), _rne_e4m3_saturating(s), np.uint8(0x7F))
+    np.testing.assert_array_equal(got, want)
+    special = np.array([np.inf, np.nan], dtype=np.float32)
+    assert list(oracle.e4m3_encode(special)) == [0x7F, 0x7F]
+    # NaN fails "s <= 464" and Inf exceeds it: both take the 0x7F branch, as the reference does
+    assert not (special <= np.float32(464.0)).any()
