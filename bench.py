@@ -21,6 +21,7 @@ round) as restated by the CPU oracle, on this host's cores, on a bounded row sam
 """
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -235,61 +236,125 @@ def workload_config(args):
 
 
 # ------------------------------------------------------------------------------------ clocks
+_REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+            ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
+
+
 class ClockSampler:
+    """SM clock, power and clock-event (throttle) reasons of one GPU, read through NVML by a
+    background thread about every 2 ms, each sample stamped with the host clock. `window()`
+    brackets the stretch during which the GPU is busy with the timed work; `summary()` reports
+    only the samples inside a window (none under load gives `samples_under_load: 0` and no clock
+    figure, never idle readings). Falls back to `nvidia-smi -lms 100` into a temporary file when
+    NVML cannot be loaded."""
+
     def __init__(self, device_index):
         self.idx = device_index
-        self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_{device_index}.csv")
+        self.samples = []  # (t, sm_mhz, max_mhz, power_w, reasons_mask)
+        self.windows = []
+        self._stop = False
+        self._thread = None
+        self._smi = None
+        self._tmp = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.idx)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+
+    def _run(self, nv, h):
+        max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self._stop:
+            try:
+                t = time.perf_counter()
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((t, sm, max_mhz, pw, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import threading
+
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100", "-i", str(self.idx)],
-                stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
-        time.sleep(0.3)
+            nv, h = self._handle()
+            self._thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
+            self._thread.start()
+        except Exception:
+            self._start_smi()
+        time.sleep(0.05)
         return self
 
+    def _start_smi(self):
+        import tempfile
+
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active")
+        try:
+            self._tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self._smi = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100", "-i", str(self.idx)],
+                stdout=self._tmp, stderr=subprocess.DEVNULL)
+            self._smi_t0 = time.perf_counter()
+        except OSError:
+            self._smi = None
+
+    @contextlib.contextmanager
+    def window(self):
+        t0 = time.perf_counter()
+        try:
+            yield
+        finally:
+            self.windows.append((t0, time.perf_counter()))
+
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        if self._smi is not None:
+            self._smi.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._smi.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.f.close()
+                self._smi.kill()
+            self._tmp.flush()
+            self._tmp.seek(0)
+            # nvidia-smi lines carry no timestamps: spread them evenly from its start
+            for i, line in enumerate(self._tmp.read().splitlines()):
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    rs = int(parts[3], 16)
+                    self.samples.append((self._smi_t0 + 0.1 * i, float(parts[0]), float(parts[1]), float(parts[2]), rs))
+                except (ValueError, IndexError):
+                    continue
+            self._tmp.close()
+            os.unlink(self._tmp.name)
 
     def summary(self):
-        if self.proc is None:
-            return None
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-                except ValueError:
-                    continue
-        if not rows:
-            return None
-        loaded = [r for r in rows if r[2] > 300.0] or rows
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower().startswith("active")})
-        return {
-            "sm_mhz": statistics.median(r[0] for r in loaded),
-            "sm_max_mhz": max(r[1] for r in loaded),
-            "power_w_max": max(r[2] for r in loaded),
-            "samples": len(loaded),
+        inside = [s for s in self.samples if any(a <= s[0] <= b for a, b in self.windows)]
+        span = sum(b - a for a, b in self.windows)
+        out = {"samples_under_load": len(inside), "window_ms": span * 1e3,
+               "source": "nvml every ~2 ms" if self._thread is not None else "nvidia-smi -lms 100"}
+        if not inside:
+            out["note"] = "no sample fell inside the busy window"
+            return out
+        reasons = sorted({name for s in inside for name, bit in _REASONS if s[4] & bit})
+        out.update({
+            "sm_mhz": statistics.median(s[1] for s in inside),
+            "sm_min_mhz": min(s[1] for s in inside),
+            "sm_max_mhz": max(s[2] for s in inside),
+            "power_w_max": max(s[3] for s in inside),
             "reasons": reasons,
-        }
+        })
+        return out
 
 
 # ---------------------------------------------------------------------------------- GPU path
@@ -363,6 +428,9 @@ def run_ours(args):
         for i in range(n_sets):  # compile-free warm path, also sets kernel attributes
             step(i)
         torch.cuda.synchronize()
+        # One graph per input set (single-launch timing), and one graph holding a launch for every
+        # set in a row: consecutive GEMMs in it chain through programmatic dependent launch (the
+        # gemm() default), each one step of the timed region.
         graphs = []
         stream = torch.cuda.Stream(dev)
         stream.wait_stream(torch.cuda.current_stream(dev))
@@ -372,35 +440,43 @@ def run_ours(args):
                 with torch.cuda.graph(gr, stream=stream):
                     step(i)
                 graphs.append(gr)
+            chain = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(chain, stream=stream):
+                for i in range(n_sets):
+                    step(i)
         torch.cuda.current_stream(dev).wait_stream(stream)
         torch.cuda.synchronize()
 
-        for i in range(args.warmup):
-            graphs[i % n_sets].replay()
-        torch.cuda.synchronize()
         cur = torch.cuda.current_stream(dev)
-        # single launches before the long run (burst clocks), each bracketed by events
-        lat = []
-        for i in range(min(args.steps, 32)):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(cur)
-            graphs[i % n_sets].replay()
-            e1.record(cur)
-            lat.append((e0, e1))
-        torch.cuda.synchronize()
-        launch_ms = statistics.median(a.elapsed_time(b) for a, b in lat)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clocks:
-            start.record(cur)
-            for i in range(args.steps):
-                graphs[i % n_sets].replay()
-            end.record(cur)
+            with clocks.window():
+                for i in range(args.warmup):
+                    graphs[i % n_sets].replay()
+                torch.cuda.synchronize()
+                # single launches before the timed run (burst clocks), each bracketed by events
+                lat = []
+                for i in range(min(args.steps, 32)):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(cur)
+                    graphs[i % n_sets].replay()
+                    e1.record(cur)
+                    lat.append((e0, e1))
+                torch.cuda.synchronize()
+            launch_ms = statistics.median(a.elapsed_time(b) for a, b in lat)
+            if world > 1:
+                dist.barrier()
             torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with clocks.window():
+                start.record(cur)
+                for _ in range(args.steps // n_sets):
+                    chain.replay()
+                for i in range(args.steps % n_sets):
+                    graphs[i].replay()
+                end.record(cur)
+                torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
         ms_local = start.elapsed_time(end)
     status = g3.device_status()
     if status:
@@ -421,7 +497,7 @@ def run_ours(args):
 
     vendor = None
     if world == 1 and not args.no_vendor:
-        vendor = time_cublaslt(sets, out_dtype, dev, M, N, K)
+        vendor = time_cublaslt(sets, out_dtype, dev, M, N, K, cfg)
 
     quantiser = None
     if world == 1 and not args.no_quantiser:
@@ -430,20 +506,29 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         e2e = time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world)
+        # The copies dominate this figure: say how much of a step the GEMM is and what rate the
+        # host link carried.
+        moved = e2e["h2d_bytes_per_step"] + e2e["d2h_bytes_per_step"]
+        e2e["bound"] = "host<->device copies (PCIe), not the kernels"
+        e2e["host_link_gbs"] = moved / (e2e["ms_per_step"] * 1e-3) / 1e9
+        e2e["gemm_share_of_step"] = ms_per_step / e2e["ms_per_step"]
 
-    del graphs
+    del graphs, chain
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args, M, N, K, seconds=args.cpu_seconds, warmup=1)
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
-    # The timed region is one GEMM launch per step, back to back for seconds: its average launch
-    # duration is set against the sustained peak; the burst single-launch figure is kept beside.
-    bf16_sus, _, peak_src = peaks(sustained=True)
+    # Peak pairing by the measured length of the timed region: a region shorter than a second runs
+    # at burst clocks and is set against the burst bf16 figure (x4 for dense FP4), a longer one
+    # against the sustained figure (a seconds-long loop under the same power cap).
+    long_run = ms_total >= 1000.0
+    bf16_peak, _, peak_src = peaks(sustained=long_run)
     bf16_burst, _, _ = peaks()
-    fp4_peak, fp4_burst = 4.0 * bf16_sus, 4.0 * bf16_burst
+    fp4_peak, fp4_burst = 4.0 * bf16_peak, 4.0 * bf16_burst
     achieved = 2.0 * M * N * K / (ms_per_step * 1e-3) / 1e12
     achieved_burst = 2.0 * M * N * K / (launch_ms * 1e-3) / 1e12
+    key = "bf16_tflops_sustained" if long_run else "bf16_tflops"
     line = {
         "metric": METRIC,
         "value": value,
@@ -466,13 +551,16 @@ def run_ours(args):
             "peak": fp4_peak,
             "unit": "TFLOP/s",
             "frac": achieved / fp4_peak,
-            "peak_source": (f"4 x bf16_tflops_sustained of MEASURED_PEAKS.json ({bf16_sus:.0f}); dense FP4 = 4x dense "
-                            f"BF16; achieved = the timed region's average launch ({ms_per_step * 1e3:.1f} us)"
-                            if peak_src == "measured" else f"4 x fallback sustained bf16 {bf16_sus:.0f}"),
+            "peak_source": (f"4 x {key} of MEASURED_PEAKS.json ({bf16_peak:.0f}, of measured): the timed region "
+                            f"lasted {ms_total:.1f} ms ({'>=' if long_run else '<'} 1 s); dense FP4 = 4x dense BF16; "
+                            f"achieved = its average launch ({ms_per_step * 1e3:.1f} us)"
+                            if peak_src == "measured" else f"4 x fallback {'sustained ' if long_run else ''}bf16 "
+                            f"{bf16_peak:.0f} (of fallback)"),
             "burst": {"us_per_launch": launch_ms * 1e3, "achieved": achieved_burst, "peak": fp4_burst,
                       "frac": achieved_burst / fp4_burst,
-                      "note": "median single launch before the long run, against 4 x bf16_tflops (burst)"},
+                      "note": "median single launch before the timed run, against 4 x bf16_tflops (burst)"},
             "frac_of_nominal_9pf": achieved / NOMINAL_FP4_DENSE_TFLOPS,
+            "frac_of_cublaslt": (achieved / (vendor["pflops"] * 1e3)) if vendor and "pflops" in vendor else None,
             "traffic": profiled_traffic(M, N, K, args.out_dtype),
             "algorithmic_bytes": M * K // 2 + N * K // 2 + (M + N) * K // 16 + 2 * M * N,
         },
@@ -638,10 +726,13 @@ def time_fused_gather(sets, world, dev, M, N, K, out_dtype, cfg):
             "layout": "row-major [M, world*N] on every rank, written by the GEMM epilogue (peer stores)"}
 
 
-def time_cublaslt(sets, out_dtype, dev, M, N, K):
+def time_cublaslt(sets, out_dtype, dev, M, N, K, cfg):
     """cuBLASLt's NVFP4 GEMM on the same rotating inputs (CUDA-graph replays, CUDA events): the
-    vendor baseline on this B200. Outputs are bit-identical to gemm3_b200.gemm (tests/)."""
+    vendor baseline on this B200. Its output on the last input set is compared with
+    gemm3_b200.gemm's on the same set (bit equality and the count of differing elements)."""
     import torch
+
+    import gemm3_b200 as g3
 
     try:
         from gemm3_b200.cublaslt import gemm_cublaslt
@@ -680,8 +771,16 @@ def time_cublaslt(sets, out_dtype, dev, M, N, K):
     torch.cuda.synchronize()
     us = statistics.median(a.elapsed_time(b) for a, b in lat) * 1e3
     del graphs
-    return {"impl": "cuBLASLt (same GPU, same inputs, outputs bit-identical)", "us_per_gemm": us,
-            "pflops": 2.0 * M * N * K / (us * 1e-6) / 1e15}
+    last = len(sets) - 1
+    step(last)
+    a_q, b_q, a_sf, b_sf, alpha = sets[last]
+    ours = g3.gemm(a_q, b_q, a_sf, b_sf, alpha=alpha, out_dtype=out_dtype, config=cfg)
+    torch.cuda.synchronize()
+    differ = int((ours != c).sum().item())
+    return {"impl": "cuBLASLt (same GPU, same inputs)", "us_per_gemm": us,
+            "pflops": 2.0 * M * N * K / (us * 1e-6) / 1e15,
+            "output_check": {"bit_identical": differ == 0, "elements_differing": differ,
+                             "compared": f"last input set, {M}x{N} {str(out_dtype).split('.')[-1]}"}}
 
 
 def time_e2e(args, M, N, K, out_dtype, cfg, dev, rank, world):

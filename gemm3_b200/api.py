@@ -153,7 +153,8 @@ def _launch_config(m, k, cfg, attrs, pdl=0):
     # 256: CTA-pair kernel; 128: one CTA per 128x256 tile; (128, 128): weight-streaming kernel
     c.tile_m = 256 if cfg.tile[0] == 256 else 128
     c.tile_n = cfg.tile[1]
-    c.pdl = pdl if cfg.tile == (128, 128) else 0
+    c.pdl = pdl
+    c.a_share = 0
     m_tiles = -(-m // 128)
     s = int(attrs.get("fast_swz", 1) or 1)
     if s > 1:
@@ -208,9 +209,12 @@ def gemm(
         alpha: optional float32 tensor with one element; defaults to 1.0.
         out: optional [M, N] output of out_dtype.
         config: a presets.Config; defaults to presets.config_for(M, N, K).
-        enable_pdl: launch the weight-streaming kernel (tile (128, 128), the M <= 128 preset) with
-            programmatic dependent launch: its set-up overlaps the tail of the preceding kernel
-            and every load waits for that kernel. The other kernels launch plainly.
+        enable_pdl: launch with programmatic dependent launch (nvfp4_gemm_cute/kernel.py:524):
+            the kernel's set-up (barriers, TMEM, tensor-map prefetch) overlaps the tail of the
+            preceding kernel on the stream, and it reads and writes global memory only after
+            that kernel has completed. This holds for every kernel (CTA-pair, one-CTA,
+            weight-streaming); the CTA-pair and one-CTA kernels also let the next PDL launch on
+            the stream start its set-up as soon as SMs free up.
 
     Requires N % 64 == 0 and K % 64 == 0. Shape, attribute and preset checks raise ValueError
     before any GPU work.

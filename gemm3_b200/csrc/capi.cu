@@ -11,6 +11,7 @@
 #include "../../include/nvfp4_gemm.h"
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
+#include "gemm_quad_kernel.cuh"
 #include "gemm_stream_kernel.cuh"
 #include "quant_kernel.cuh"
 
@@ -41,6 +42,7 @@ struct DeviceCache {
   bool gemm_attr_set = false;
   bool stream_attr_set = false;
   int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
+  int quad_clusters = 0;  // co-resident 4-CTA clusters of the A-sharing kernel
   // co-resident 256-thread quantiser blocks per SM, per input dtype and QuantKind
   int quant_blocks[3][3] = {{0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
 };
@@ -138,6 +140,20 @@ int ensure_gemm_attributes(DeviceCache* d) {
     n = d->sm_count / 2;
   }
   d->pair_clusters = n;
+  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_quad_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g3::kQuadSmemBytes));
+  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_quad_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g3::kQuadSmemBytes));
+  lc.gridDim = dim3(4 * (d->sm_count / 4), 1, 1);
+  lc.blockDim = dim3(g3::kQuadThreads, 1, 1);
+  lc.dynamicSmemBytes = g3::kQuadSmemBytes;
+  attr.val.clusterDim.x = 4;
+  int nq = 0;
+  if (cudaOccupancyMaxActiveClusters(&nq, g3::nvfp4_gemm_quad_kernel<true>, &lc) != cudaSuccess || nq < 1) {
+    (void)cudaGetLastError();
+    nq = d->sm_count / 4;
+  }
+  d->quad_clusters = nq;
   d->gemm_attr_set = true;
   return NVFP4_OK;
 }
@@ -387,13 +403,15 @@ int nvfp4_max_active_clusters(int32_t cluster_size, int32_t* out) {
   rc = device_cache(dev, &d);
   if (rc != NVFP4_OK) return rc;
   if (d->cc_major != 10) return NVFP4_ERR_UNSUPPORTED;
-  auto kern = g3::nvfp4_gemm_kernel<true>;
-  G3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kGemmSmemBytes));
+  // The kernel gemm() launches by default (tile 256x256): the CTA-pair kernel, with its thread
+  // count and shared memory; its own launches use clusters of 2.
+  auto kern = g3::nvfp4_gemm_pair_kernel<true>;
+  G3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPairSmemBytes));
   if (cluster_size > 8) G3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster_size * d->sm_count, 1, 1);
-  cfg.blockDim = dim3(g3::kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = g3::kGemmSmemBytes;
+  cfg.blockDim = dim3(g3::kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = g3::kPairSmemBytes;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
   attr.val.clusterDim.x = cluster_size;
@@ -432,11 +450,13 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
       (def.tile_n != 0 && def.tile_n != 256 && def.tile_n != 128))
     return NVFP4_ERR_INVALID_VALUE;
   if (def.pdl < 0 || def.pdl > 2) return NVFP4_ERR_INVALID_VALUE;
+  if (def.a_share < 0 || def.a_share > 2) return NVFP4_ERR_INVALID_VALUE;
   if (def.tile_n == 128) {
     if (def.tile_m != 128 || m > g3::kStreamMaxM) return NVFP4_ERR_INVALID_VALUE;
     return launch_stream(a, b, sfa, sfb, out, alpha, m, n, k, out_dtype, def, status, stream);
   }
   const bool pair = def.tile_m != 128;
+  const bool quad = pair && def.a_share == 2;
   if (def.raster_band < 0) return NVFP4_ERR_INVALID_VALUE;
 
   int dev = 0;
@@ -480,7 +500,8 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
   p.sf_kblocks = static_cast<int>(k / 64);
   p.a_box_bytes = static_cast<int>(a_box_rows) * g3::kTileKBytes;
   p.n_rowblocks = static_cast<int>((n + 127) / 128);
-  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  // the A-sharing kernel walks column pairs of tiles, one per cluster of two CTA pairs
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * (quad ? (p.n_tiles + 1) / 2 : p.n_tiles);
   if (tiles > INT32_MAX) return NVFP4_ERR_INVALID_VALUE;
   p.num_tiles = static_cast<int>(tiles);
   // raster_band counts 128-row tiles; the pair kernel's tiles are 256 rows
@@ -498,22 +519,47 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
   rc = ensure_gemm_attributes(d);
   if (rc != NVFP4_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (pair) {
+  // With cfg->pdl != 0 both kernels launch with programmatic stream serialisation: they wait for
+  // the preceding kernel on the device (griddepcontrol.wait) instead of at launch. They read
+  // and write nothing global before that wait, so modes 1 and 2 act the same here.
+  cudaLaunchAttribute attrs[2];
+  int n_attrs = 0;
+  if (def.pdl != 0) {
+    attrs[n_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n_attrs].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attrs;
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.stream = s;
+  lc.attrs = attrs;
+  if (quad) {
+    int clusters = d->quad_clusters;
+    if (def.max_ctas > 0 && def.max_ctas / 4 < clusters) clusters = def.max_ctas / 4 > 0 ? def.max_ctas / 4 : 1;
+    if (clusters > p.num_tiles) clusters = p.num_tiles;
+    lc.gridDim = dim3(4 * clusters, 1, 1);
+    lc.blockDim = dim3(g3::kQuadThreads, 1, 1);
+    lc.dynamicSmemBytes = g3::kQuadSmemBytes;
+    attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
+    attrs[n_attrs].val.clusterDim.x = 4;
+    attrs[n_attrs].val.clusterDim.y = 1;
+    attrs[n_attrs].val.clusterDim.z = 1;
+    lc.numAttrs = n_attrs + 1;
+    if (out_dtype == NVFP4_DTYPE_BF16)
+      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_quad_kernel<true>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
+    else
+      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_quad_kernel<false>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
+  } else if (pair) {
     int pairs = d->pair_clusters;
     if (def.max_ctas > 0 && def.max_ctas / 2 < pairs) pairs = def.max_ctas / 2 > 0 ? def.max_ctas / 2 : 1;
     if (pairs > p.num_tiles) pairs = p.num_tiles;
-    cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(2 * pairs, 1, 1);
     lc.blockDim = dim3(g3::kPairThreads, 1, 1);
     lc.dynamicSmemBytes = g3::kPairSmemBytes;
-    lc.stream = s;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    lc.attrs = &attr;
-    lc.numAttrs = 1;
+    attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
+    attrs[n_attrs].val.clusterDim.x = 2;
+    attrs[n_attrs].val.clusterDim.y = 1;
+    attrs[n_attrs].val.clusterDim.z = 1;
+    lc.numAttrs = n_attrs + 1;
     if (out_dtype == NVFP4_DTYPE_BF16)
       G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_pair_kernel<true>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
     else
@@ -522,10 +568,14 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
     int ctas = d->sm_count;
     if (def.max_ctas > 0 && def.max_ctas < ctas) ctas = def.max_ctas;
     if (ctas > p.num_tiles) ctas = p.num_tiles;
+    lc.gridDim = dim3(ctas, 1, 1);
+    lc.blockDim = dim3(g3::kGemmThreads, 1, 1);
+    lc.dynamicSmemBytes = g3::kGemmSmemBytes;
+    lc.numAttrs = n_attrs;
     if (out_dtype == NVFP4_DTYPE_BF16)
-      g3::nvfp4_gemm_kernel<true><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_kernel<true>, tmap_a, tmap_b, p));
     else
-      g3::nvfp4_gemm_kernel<false><<<ctas, g3::kGemmThreads, g3::kGemmSmemBytes, s>>>(tmap_a, tmap_b, p);
+      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_kernel<false>, tmap_a, tmap_b, p));
   }
   G3_CUDA(cudaGetLastError());
   return NVFP4_OK;

@@ -182,6 +182,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: set-up overlaps the preceding kernel; global memory is
+  // touched only after it has completed (as in the CTA-pair kernel).
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer

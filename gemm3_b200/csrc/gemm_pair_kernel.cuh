@@ -128,6 +128,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch (nvfp4_gemm_cute/kernel.py:524, :910-911): the set-up above
+  // overlaps the tail of the preceding kernel on the stream; every thread waits here, before
+  // its first global read or write, until that kernel has completed and its memory is visible
+  // (at once for a plain launch). The next kernel may be scheduled at once: with this CTA's
+  // shared memory it can only become resident on SMs that this grid has left.
+  griddep_launch_dependents();
+  griddep_wait();
 
   // CTA 0's barriers as seen from either CTA of the pair.
   const uint32_t full0 = mapa_shared(smem_u32(full), 0);

@@ -21,7 +21,8 @@
 // leaves the normal range, which holds for |xb| >= 2^-100. Below that |q| < 2^-91, so the
 // magnitude code is 0 however q rounds, and the sign bit is decided from xb and the scale
 // directly (e2m1_pack16). Blocks whose every |xb| is at least 2^-100 (the common case) take
-// e2m1_pack8_signed, where the conversions of the signed quotient set the sign bits.
+// e2m1_pack8_fast, which converts x * (gs / d) slightly scaled down and up, and forms the exact
+// quotient only for the rare element that lies next to a rounding tie.
 //
 // The codes themselves come from the hardware E2M1 conversion (round-to-nearest-even); the
 // reference's tie rule is applied exactly by a check that sends only elements next to a rounding
@@ -156,26 +157,32 @@ __device__ __forceinline__ uint2 e2m1_pack16(const float (&xb)[16], float d, flo
   return make_uint2(e2m1_pack8(xb, d, r, d_lo), e2m1_pack8(xb + 8, d, r, d_lo));
 }
 
-// e2m1_pack8 for a block whose every |xb| is at least 2^-100, in paired FP32 arithmetic (one
-// f32x2 instruction per two elements). There the quotient is the correctly rounded one and is a
-// normal float (|q| >= 2^-109), so the reference's sign test q < 0 is just the sign of xb and of
-// q; the conversions take the signed quotients and set the sign bit themselves (a negative q whose
-// magnitude rounds to 0 gives code 8, as in the reference). lo and hi carry the same sign, so
-// their codes can differ only in the magnitude bits, which the exact steps then replace.
-__device__ __forceinline__ uint32_t e2m1_pack8_signed(const float* xb, float d, float r) {
-  const float2 r2 = make_float2(r, r), nd2 = make_float2(-d, -d);
-  const float2 klo = make_float2(0x1.ffffp-1f, 0x1.ffffp-1f);     // 1 - 2^-17
-  const float2 khi = make_float2(0x1.00008p+0f, 0x1.00008p+0f);   // 1 + 2^-17
-  float q[8], lo[8], hi[8];
+// Approximate reciprocal (MUFU; at most a couple of ulps from 1/d, d a normal float).
+__device__ __forceinline__ float rcp_approx(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return r;
+}
+
+// Packed E2M1 codes of eight elements of a block whose every |xb| = |x * gs| is at least 2^-100,
+// from the raw inputs x: one paired multiply per two elements and side.
+//  - For such a block q = RN(xb / d) is a nonzero normal float with the sign of xb, so the
+//    reference's sign test q < 0 is the sign of x * gs, which the conversions set themselves (a
+//    negative q whose magnitude rounds to 0 gives code 8, as in the reference).
+//  - lo = x * RN(RN(gs * ~1/d) * (1 - 2^-17)) and hi likewise with (1 + 2^-17) are within a few
+//    ulps (relative 6e-7) of q * (1 -+ 2^-17), while the reference's rounding rule differs from
+//    round-to-nearest-even only within 2.2e-6 of a tie. So where the hardware conversions of lo
+//    and hi agree, no tie lies within 5e-6 of q and that code is the reference's.
+//  - An element whose two conversions differ takes the exact path: xb = RN(x * gs), the
+//    correctly rounded quotient by Markstein's correction with r = RN(1 / d), and the threshold
+//    steps. Only the magnitude bits are replaced; lo and hi carry the same sign.
+__device__ __forceinline__ uint32_t e2m1_pack8_fast(const float* x, float gs, float d, float clo, float chi) {
+  const float2 clo2 = make_float2(clo, clo), chi2 = make_float2(chi, chi);
+  float lo[8], hi[8];
 #pragma unroll
   for (int i = 0; i < 8; i += 2) {
-    const float2 x = make_float2(xb[i], xb[i + 1]);
-    const float2 q1 = __fmul2_rn(x, r2);
-    const float2 rem = __ffma2_rn(q1, nd2, x);
-    const float2 qq = __ffma2_rn(rem, r2, q1);
-    const float2 l = __fmul2_rn(qq, klo), h = __fmul2_rn(qq, khi);
-    q[i] = qq.x;
-    q[i + 1] = qq.y;
+    const float2 xx = make_float2(x[i], x[i + 1]);
+    const float2 l = __fmul2_rn(xx, clo2), h = __fmul2_rn(xx, chi2);
     lo[i] = l.x;
     lo[i + 1] = l.y;
     hi[i] = h.x;
@@ -184,10 +191,16 @@ __device__ __forceinline__ uint32_t e2m1_pack8_signed(const float* xb, float d, 
   uint32_t w = cvt_e2m1x8(lo);
   const uint32_t near_tie = w ^ cvt_e2m1x8(hi);
   if (near_tie != 0u) {
+    const float r = __frcp_rn(d);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if ((near_tie >> (4 * i)) & 0xFu)
-        w = (w & ~(0x7u << (4 * i))) | (e2m1_mag_code_steps(fabsf(q[i])) << (4 * i));
+      if ((near_tie >> (4 * i)) & 0xFu) {
+        const float xb = __fmul_rn(x[i], gs);
+        const float q1 = __fmul_rn(xb, r);
+        const float rem = __fmaf_rn(q1, -d, xb);
+        const float q = __fmaf_rn(rem, r, q1);
+        w = (w & ~(0x7u << (4 * i))) | (e2m1_mag_code_steps(fabsf(q)) << (4 * i));
+      }
   }
   return w;
 }
@@ -278,21 +291,19 @@ __device__ __forceinline__ float resolve_global_scale(const QuantParams& p) {
 }
 
 // The scale byte and packed codes of one 16-element block of input values.
+//  - The block amax and smallest magnitude are taken over the raw |x| and scaled once: RN(. * |gs|)
+//    is monotone, so RN(max|x| * |gs|) = max |RN(x * gs)| = the reference's amax of xb (NaN and
+//    infinities propagate the same way), and likewise for the minimum.
+//  - Blocks whose every |xb| is at least 2^-100 (the common case) take e2m1_pack8_fast; blocks
+//    holding a zero or a smaller magnitude take the general path, which forms xb and decides
+//    signs without the quotient.
 template <int kInDtype>
 __device__ __forceinline__ uint32_t quantize_values(const RawBlock<kInDtype>& rb, float gs, int div_mode, uint2& codes) {
   const float inv6 = 0.166666672f;  // fl(1/6): what torch on CUDA multiplies by for "/ 6.0"
   float v[16];
   unpack_raw<kInDtype>(rb, v);
-  const float2 gs2 = make_float2(gs, gs);
-#pragma unroll
-  for (int i = 0; i < 16; i += 2) {
-    const float2 xb = __fmul2_rn(make_float2(v[i], v[i + 1]), gs2);
-    v[i] = xb.x;
-    v[i + 1] = xb.y;
-  }
-  // amax is NaN if any element is NaN and Inf if one is infinite: the reference's scale is NaN
+  // A NaN element makes amax NaN and an infinite one makes it Inf: the reference's scale is NaN
   // either way (NaN amax, or Inf / 6 overflowing E4M3), and e4m3_encode_nonneg maps both to 0x7F.
-  // mn, the smallest magnitude, picks the arithmetic below.
   float amax = max3_nan(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
   float mn = min3(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
 #pragma unroll
@@ -302,16 +313,31 @@ __device__ __forceinline__ uint32_t quantize_values(const RawBlock<kInDtype>& rb
   }
   amax = max_nan(amax, fabsf(v[15]));
   mn = fminf(mn, fabsf(v[15]));
+  const float ags = fabsf(gs);
+  amax = __fmul_rn(amax, ags);
+  mn = __fmul_rn(mn, ags);
   const float s = div_mode == 0 ? __fmul_rn(amax, inv6) : __fdiv_rn(amax, 6.0f);
   const uint32_t sf = e4m3_encode_nonneg(s);
   const float denom = e4m3_decode(sf);
-  // else q = 0 for every element: code 0 (a NaN scale included). Blocks holding a zero or a
-  // magnitude below 2^-100 take the general path, which decides signs without the quotient.
+  // else q = 0 for every element: code 0 (a NaN scale included)
   codes = make_uint2(0u, 0u);
   if (denom > 0.0f) {
-    const float rd = __frcp_rn(denom);
-    codes = mn >= 0x1p-100f ? make_uint2(e2m1_pack8_signed(v, denom, rd), e2m1_pack8_signed(v + 8, denom, rd))
-                            : e2m1_pack16(v, denom, rd);
+    // g = gs / d must be a normal float for the products x * g to keep their precision.
+    const float g = __fmul_rn(gs, rcp_approx(denom));
+    if (mn >= 0x1p-100f && fabsf(g) >= 0x1p-125f && fabsf(g) <= 0x1p+125f) {
+      const float clo = __fmul_rn(g, 0x1.ffffp-1f);   // 1 - 2^-17
+      const float chi = __fmul_rn(g, 0x1.00008p+0f);  // 1 + 2^-17
+      codes = make_uint2(e2m1_pack8_fast(v, gs, denom, clo, chi), e2m1_pack8_fast(v + 8, gs, denom, clo, chi));
+    } else {
+      const float2 gs2 = make_float2(gs, gs);
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const float2 xb = __fmul2_rn(make_float2(v[i], v[i + 1]), gs2);
+        v[i] = xb.x;
+        v[i + 1] = xb.y;
+      }
+      codes = e2m1_pack16(v, denom, __frcp_rn(denom));
+    }
   }
   return sf;
 }

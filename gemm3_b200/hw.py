@@ -12,6 +12,10 @@ from . import _lib
 def get_max_active_clusters(cluster_size: int) -> int:
     """Return how many clusters of cluster_size CTAs of the GEMM kernel fit on the current GPU.
 
+    The kernel is the one gemm() launches by default, the CTA-pair kernel (tile (256, 256)); with
+    cluster_size 2 the answer is the number of CTA pairs its persistent grid holds (74 on a B200
+    whose 148 SMs all pair up).
+
     Uses cudaOccupancyMaxActiveClusters through the extension; if the occupancy query fails it
     falls back to the SM count divided by the cluster size, like the reference.
     """

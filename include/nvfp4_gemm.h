@@ -68,10 +68,18 @@ typedef struct nvfp4_gemm_config {
   int32_t epi_store_pace_ns;     /* pause between output 32-column chunks (0 = none) */
   int32_t tma_b_first;           /* issue the B load before A in each stage */
   int32_t max_ctas;              /* cap on persistent CTAs (0 = one per SM) */
-  int32_t pdl;                   /* programmatic dependent launch, weight-streaming kernel only (others
-                                    launch plainly): 0 off; 1 every load waits for the preceding kernel;
-                                    2 B and its scales are loaded before that wait, A, its scales and
-                                    alpha after it (B must not be written by the preceding kernel) */
+  int32_t pdl;                   /* programmatic dependent launch (nvfp4_gemm_cute/kernel.py:524):
+                                    0 off; 1 the kernel's set-up overlaps the preceding kernel and
+                                    every global read or write waits for it (griddepcontrol.wait);
+                                    2 as 1, except that the weight-streaming kernel loads B and its
+                                    scales before that wait (B must not be written by the preceding
+                                    kernel; the other kernels treat 2 as 1). The CTA-pair and one-CTA
+                                    kernels also let the next PDL launch start early. */
+  int32_t a_share;               /* tile 256x256 only: 0 or 1, one CTA pair per cluster; 2, clusters of two
+                                    CTA pairs on neighbouring column tiles that load half of their common
+                                    A tiles each and pass it to the other through distributed shared
+                                    memory (the B200 counterpart of the reference's cluster N extent,
+                                    presets.py Config.cluster[1], which shares A by TMA multicast) */
 } nvfp4_gemm_config;
 
 /*
@@ -212,8 +220,10 @@ int nvfp4_dequantize(const void* packed, const void* sf_linear, int64_t rows, in
  * (nvfp4_gemm_cute/quant.py:31-38). */
 int nvfp4_swizzle_sf(const void* sf_linear, int64_t rows, int64_t cols, void* out, void* stream);
 
-/* How many clusters of cluster_size CTAs of the GEMM kernel can be co-resident on the current
- * device. Replaces get_max_active_clusters (nvfp4_gemm_cute/hw.py:8-22). */
+/* How many clusters of cluster_size CTAs of the default GEMM kernel (the CTA-pair kernel that
+ * gemm() launches for tile 256x256, with its threads and shared memory) can be co-resident on the
+ * current device; cluster_size 2 is the pair grid it launches. Replaces get_max_active_clusters
+ * (nvfp4_gemm_cute/hw.py:8-22). */
 int nvfp4_max_active_clusters(int32_t cluster_size, int32_t* out);
 
 /* SM count, compute capability and L2 size of `device`. */

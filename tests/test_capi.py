@@ -62,6 +62,12 @@ def test_argument_validation_without_gpu(L):
     assert L.nvfp4_gemm_run(p, p, p, p, p, p, 128, 128, 128, 2, None, None, None) == 1
     # misaligned A
     assert L.nvfp4_gemm_run(ctypes.c_void_p((1 << 20) + 8), p, p, p, p, p, 128, 128, 128, 0, None, None, None) == 2
+    # out-of-range config fields
+    for field, bad in (("a_share", 3), ("pdl", 3), ("tile_n", 64)):
+        cfg = _lib.GemmConfig()
+        cfg.struct_size = ctypes.sizeof(cfg)
+        setattr(cfg, field, bad)
+        assert L.nvfp4_gemm_run(p, p, p, p, p, p, 128, 128, 128, 0, ctypes.byref(cfg), None, None) == 1, field
     # quantiser: K not a multiple of 16, bad gs_mode
     assert L.nvfp4_quantize(p, 1, 4, 24, 1.0, None, 0, 0, p, p, None, None, None) == 1
     assert L.nvfp4_quantize(p, 1, 4, 32, 1.0, None, 1, 0, p, p, None, None, None) == 1

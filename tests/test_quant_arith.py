@@ -148,3 +148,43 @@ def test_saturating_e4m3_with_overflow_compare_matches_reference_encode():
     assert list(oracle.e4m3_encode(special)) == [0x7F, 0x7F]
     # NaN fails "s <= 464" and Inf exceeds it: both take the 0x7F branch, as the reference does
     assert not (special <= np.float32(464.0)).any()
+
+
+def test_fast_path_from_raw_inputs_matches_reference():
+    """The common-case code path converts x * RN(RN(gs * r) * (1 -/+ 2^-17)) with r an
+    approximate reciprocal of the scale d (within a few ulps of 1/d), straight from the raw input
+    x; where the two conversions agree it keeps that code, which must be the reference's code of
+    q = RN(RN(x * gs) / d). Checked with r moved up to 3 ulps either side of RN(1/d), on every
+    E4M3 scale significand over several exponents, with inputs drawn at random and on windows
+    of x around each rounding tie of q."""
+    rng = np.random.default_rng(7)
+    eps = np.float32(2.0**-17)
+    ties = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], dtype=np.float32)
+    checked = fallback = 0
+    for exp in (-9, -3, 0, 4, 8):
+        for m in range(8):
+            d = np.float32((1 + m / 8) * 2.0**exp)
+            for gs in (np.float32(1.0), np.float32(2688.0 / 3.7), np.float32(-0.8125), np.float32(41.3)):
+                q_near = (ties[:, None] * (1 + np.linspace(-4e-5, 4e-5, 801)[None, :])).ravel()
+                x = np.concatenate([
+                    (q_near * d / gs).astype(np.float32),
+                    (rng.uniform(-6.4, 6.4, 20000) * d / gs).astype(np.float32),
+                ])
+                xb = (x * gs).astype(np.float32)
+                keep = np.abs(xb) >= np.float32(2.0**-100)
+                x, xb = x[keep], xb[keep]
+                q = (xb / d).astype(np.float32)
+                want = oracle_codes(np.abs(q).view(np.uint32))
+                r0 = np.float32(1.0) / d
+                for du in range(-3, 4):
+                    r = (r0.view(np.uint32) + np.uint32(du & 0xFFFFFFFF)).view(np.float32) if du >= 0 else \
+                        (r0.view(np.uint32) - np.uint32(-du)).view(np.float32)
+                    g = np.float32(gs * r)
+                    lo = np.abs((x * np.float32(g * (np.float32(1) - eps))).astype(np.float32))
+                    hi = np.abs((x * np.float32(g * (np.float32(1) + eps))).astype(np.float32))
+                    clo, chi = _rne_e2m1(lo), _rne_e2m1(hi)
+                    fast = clo == chi
+                    np.testing.assert_array_equal(clo[fast], want[fast])
+                    checked += int(fast.sum())
+                    fallback += int((~fast).sum())
+    assert checked > 10 * fallback
