@@ -66,7 +66,6 @@ class GemmConfig(ctypes.Structure):
         ("tma_b_first", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
         ("pdl", ctypes.c_int32),
-        ("a_share", ctypes.c_int32),
     ]
 
 

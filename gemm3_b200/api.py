@@ -154,7 +154,6 @@ def _launch_config(m, k, cfg, attrs, pdl=0):
     c.tile_m = 256 if cfg.tile[0] == 256 else 128
     c.tile_n = cfg.tile[1]
     c.pdl = pdl
-    c.a_share = 0
     m_tiles = -(-m // 128)
     s = int(attrs.get("fast_swz", 1) or 1)
     if s > 1:

@@ -18,7 +18,7 @@ LIB_NAME = "libgemm3_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = [os.path.join(CSRC, "capi.cu")]
 DEPENDS = SOURCES + [
-    os.path.join(CSRC, f) for f in ("ptx.cuh", "gemm_kernel.cuh", "gemm_pair_kernel.cuh", "gemm_quad_kernel.cuh", "gemm_stream_kernel.cuh", "quant_kernel.cuh")
+    os.path.join(CSRC, f) for f in ("ptx.cuh", "gemm_kernel.cuh", "gemm_pair_kernel.cuh", "gemm_stream_kernel.cuh", "quant_kernel.cuh")
 ] + [os.path.join(REPO_DIR, "include", "nvfp4_gemm.h")]
 
 NVCC_FLAGS = [

@@ -11,7 +11,6 @@
 #include "../../include/nvfp4_gemm.h"
 #include "gemm_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
-#include "gemm_quad_kernel.cuh"
 #include "gemm_stream_kernel.cuh"
 #include "quant_kernel.cuh"
 
@@ -42,7 +41,6 @@ struct DeviceCache {
   bool gemm_attr_set = false;
   bool stream_attr_set = false;
   int pair_clusters = 0;  // co-resident CTA pairs of the pair kernel
-  int quad_clusters = 0;  // co-resident 4-CTA clusters of the A-sharing kernel
   // co-resident 256-thread quantiser blocks per SM, per input dtype and QuantKind
   int quant_blocks[3][3] = {{0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
 };
@@ -140,20 +138,6 @@ int ensure_gemm_attributes(DeviceCache* d) {
     n = d->sm_count / 2;
   }
   d->pair_clusters = n;
-  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_quad_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               g3::kQuadSmemBytes));
-  G3_CUDA(cudaFuncSetAttribute(g3::nvfp4_gemm_quad_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               g3::kQuadSmemBytes));
-  lc.gridDim = dim3(4 * (d->sm_count / 4), 1, 1);
-  lc.blockDim = dim3(g3::kQuadThreads, 1, 1);
-  lc.dynamicSmemBytes = g3::kQuadSmemBytes;
-  attr.val.clusterDim.x = 4;
-  int nq = 0;
-  if (cudaOccupancyMaxActiveClusters(&nq, g3::nvfp4_gemm_quad_kernel<true>, &lc) != cudaSuccess || nq < 1) {
-    (void)cudaGetLastError();
-    nq = d->sm_count / 4;
-  }
-  d->quad_clusters = nq;
   d->gemm_attr_set = true;
   return NVFP4_OK;
 }
@@ -450,13 +434,11 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
       (def.tile_n != 0 && def.tile_n != 256 && def.tile_n != 128))
     return NVFP4_ERR_INVALID_VALUE;
   if (def.pdl < 0 || def.pdl > 2) return NVFP4_ERR_INVALID_VALUE;
-  if (def.a_share < 0 || def.a_share > 2) return NVFP4_ERR_INVALID_VALUE;
   if (def.tile_n == 128) {
     if (def.tile_m != 128 || m > g3::kStreamMaxM) return NVFP4_ERR_INVALID_VALUE;
     return launch_stream(a, b, sfa, sfb, out, alpha, m, n, k, out_dtype, def, status, stream);
   }
   const bool pair = def.tile_m != 128;
-  const bool quad = pair && def.a_share == 2;
   if (def.raster_band < 0) return NVFP4_ERR_INVALID_VALUE;
 
   int dev = 0;
@@ -500,8 +482,7 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
   p.sf_kblocks = static_cast<int>(k / 64);
   p.a_box_bytes = static_cast<int>(a_box_rows) * g3::kTileKBytes;
   p.n_rowblocks = static_cast<int>((n + 127) / 128);
-  // the A-sharing kernel walks column pairs of tiles, one per cluster of two CTA pairs
-  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * (quad ? (p.n_tiles + 1) / 2 : p.n_tiles);
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
   if (tiles > INT32_MAX) return NVFP4_ERR_INVALID_VALUE;
   p.num_tiles = static_cast<int>(tiles);
   // raster_band counts 128-row tiles; the pair kernel's tiles are 256 rows
@@ -532,23 +513,7 @@ static int gemm_run_impl(const void* a, const void* b, const void* sfa, const vo
   cudaLaunchConfig_t lc = {};
   lc.stream = s;
   lc.attrs = attrs;
-  if (quad) {
-    int clusters = d->quad_clusters;
-    if (def.max_ctas > 0 && def.max_ctas / 4 < clusters) clusters = def.max_ctas / 4 > 0 ? def.max_ctas / 4 : 1;
-    if (clusters > p.num_tiles) clusters = p.num_tiles;
-    lc.gridDim = dim3(4 * clusters, 1, 1);
-    lc.blockDim = dim3(g3::kQuadThreads, 1, 1);
-    lc.dynamicSmemBytes = g3::kQuadSmemBytes;
-    attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
-    attrs[n_attrs].val.clusterDim.x = 4;
-    attrs[n_attrs].val.clusterDim.y = 1;
-    attrs[n_attrs].val.clusterDim.z = 1;
-    lc.numAttrs = n_attrs + 1;
-    if (out_dtype == NVFP4_DTYPE_BF16)
-      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_quad_kernel<true>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
-    else
-      G3_CUDA(cudaLaunchKernelEx(&lc, g3::nvfp4_gemm_quad_kernel<false>, tmap_a, tmap_b, tmap_sfa, tmap_sfb, p));
-  } else if (pair) {
+  if (pair) {
     int pairs = d->pair_clusters;
     if (def.max_ctas > 0 && def.max_ctas / 2 < pairs) pairs = def.max_ctas / 2 > 0 ? def.max_ctas / 2 : 1;
     if (pairs > p.num_tiles) pairs = p.num_tiles;

@@ -75,11 +75,6 @@ typedef struct nvfp4_gemm_config {
                                     scales before that wait (B must not be written by the preceding
                                     kernel; the other kernels treat 2 as 1). The CTA-pair and one-CTA
                                     kernels also let the next PDL launch start early. */
-  int32_t a_share;               /* tile 256x256 only: 0 or 1, one CTA pair per cluster; 2, clusters of two
-                                    CTA pairs on neighbouring column tiles that load half of their common
-                                    A tiles each and pass it to the other through distributed shared
-                                    memory (the B200 counterpart of the reference's cluster N extent,
-                                    presets.py Config.cluster[1], which shares A by TMA multicast) */
 } nvfp4_gemm_config;
 
 /*

@@ -63,7 +63,7 @@ def test_argument_validation_without_gpu(L):
     # misaligned A
     assert L.nvfp4_gemm_run(ctypes.c_void_p((1 << 20) + 8), p, p, p, p, p, 128, 128, 128, 0, None, None, None) == 2
     # out-of-range config fields
-    for field, bad in (("a_share", 3), ("pdl", 3), ("tile_n", 64)):
+    for field, bad in (("pdl", 3), ("tile_n", 64)):
         cfg = _lib.GemmConfig()
         cfg.struct_size = ctypes.sizeof(cfg)
         setattr(cfg, field, bad)

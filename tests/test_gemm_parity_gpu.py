@@ -312,47 +312,3 @@ def test_back_to_back_launches_with_pdl(cuda_ext):
     assert torch.equal(c2, c2_ref)
     del gr
     assert cuda_ext.device_status() == 0
-
-
-def _gemm_c_abi(a, b, alpha, dtype, **fields):
-    """gemm through the C ABI with explicit nvfp4_gemm_config fields."""
-    import ctypes
-
-    from gemm3_b200 import _lib
-
-    m, n, k = a[0].shape[0], b[0].shape[0], a[0].shape[1] * 2
-    out = torch.empty(m, n, dtype=dtype, device="cuda")
-    cfg = _lib.GemmConfig()
-    cfg.struct_size = ctypes.sizeof(cfg)
-    for name, value in fields.items():
-        setattr(cfg, name, value)
-    status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc = _lib.lib().nvfp4_gemm_run(a[0].data_ptr(), b[0].data_ptr(), a[1].data_ptr(), b[1].data_ptr(), out.data_ptr(),
-                                   alpha.data_ptr(), m, n, k, 1 if dtype == torch.bfloat16 else 0, ctypes.byref(cfg),
-                                   status.data_ptr(), torch.cuda.current_stream().cuda_stream)
-    assert rc == 0, rc
-    torch.cuda.synchronize()
-    assert int(status.item()) == 0
-    return out
-
-
-@pytest.mark.parametrize(
-    "m,n,k",
-    [(256, 512, 512), (512, 768, 1024), (1000, 1280, 768), (4096, 4096, 4096), (3329, 6080, 2240),
-     (8192, 2048, 8192), (300, 256, 1088), (2048, 4352, 4160)],
-)
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_a_sharing_clusters_match_pair_kernel(cuda_ext, m, n, k, dtype):
-    """Clusters of two CTA pairs that pass A atoms to each other through distributed shared
-    memory (nvfp4_gemm_config.a_share = 2) give the CTA-pair kernel's bits: an odd number of
-    column tiles (the second pair's last tile is absent), ragged M, K tails of 1-7 blocks in the
-    last stage, fewer tiles than clusters, and many tiles per cluster."""
-    a = _operand(m, k, seed=m + 1)
-    b = _operand(n, k, seed=n + 2)
-    alpha = (1.0 / (a[3] * b[3])).reshape(1).float()
-    shared = _gemm_c_abi(a, b, alpha, dtype, a_share=2, raster_band=4)
-    pair = _gemm_c_abi(a, b, alpha, dtype, raster_band=4)
-    assert torch.equal(shared, pair), int((shared != pair).sum())
-    if m * n * k <= 2**31:
-        _full_check(shared, a, b, alpha, f"{m}x{n}x{k} A shared")
-    assert cuda_ext.device_status() == 0
