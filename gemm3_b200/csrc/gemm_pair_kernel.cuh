@@ -6,12 +6,13 @@
 // CTA's half of the accumulator into its own TMEM. Compared with one-CTA 128x256 tiles this halves
 // the B bytes every SM loads from L2 and reads from shared memory per FLOP.
 //
-// A stage covers K = 512 (eight 64-element blocks, eight MMAs): the single MMA-issuing thread
-// spends about 80 cycles per tcgen05 instruction plus a few hundred per stage on its wait, fence
-// and commit, against 128 cycles of tensor-pipe time per MMA, so the per-stage work has to be
-// spread over eight MMAs to keep the pipe fed. Two shared-memory rings feed the MMA: a 3-stage
-// ring of A/B stages (64 KiB per CTA) and a 2-slot ring of scale stages (12 KiB). Scales sit in
-// TMEM in two 96-column regions used alternately, independent of the A/B stage.
+// A stage covers K = 512 (eight 64-element blocks, eight MMAs, 1,032 tensor-pipe cycles: one
+// CTA-pair MMA takes 129). Two shared-memory rings feed the MMA: a 3-stage ring of A/B stages
+// (64 KiB per CTA) and a 2-slot ring of scale stages (12 KiB). Scales sit in TMEM in two
+// 96-column regions used alternately, independent of the A/B stage; the copies into a region wait
+// for the MMAs two stages back, the last readers of it. The scale copies bound the main loop: a
+// stage needs 24 tcgen05.cp (.32x128b.warpx4, 2 KiB of TMEM writes each), and while MMAs run each
+// takes about 52 cycles, about 1,240 cycles per stage.
 //
 // Roles (per CTA, 10 warps):
 //   warp 0      A/B producer, both CTAs: TMA loads of its A and B halves (128 rows x 128 B,
@@ -23,9 +24,9 @@
 //               A/B stage in both CTAs and, per tile, hands the accumulator to both epilogues;
 //   warps 3,4,9 in CTA 0, scale copies into both TMEMs (tcgen05.cp cta_group::2): warp 3 one
 //               A-scale chunk per 64-element block, warps 4 and 9 the B-scale chunks of tile
-//               rows 0-127 and 128-255. Every tcgen05 instruction costs its issuing thread about
-//               50 cycles, so the three copies and the MMA of a block are spread over four
-//               threads (with one thread for both B chunks, that thread set the pace). A copy
+//               rows 0-127 and 128-255. A copy takes its issuing thread about 51 cycles, so the
+//               three copies of a block are spread over three threads and the MMA thread issues
+//               only MMAs (with one thread for both B chunks, that thread set the pace). A copy
 //               warp hands its TMEM region to the MMA thread once the copies are issued (fence +
 //               mbarrier arrive; warp 3 first waits for the stage's A/B data) and frees the
 //               shared-memory slot through a commit when they have completed;
