@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&sf_empty[q], kPairCopyWarps);  // one commit from each copy warp (multicast to both CTAs)
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 2 * 4 * 32);  // every epilogue thread of both CTAs
+    mbar_init(acc_empty, 2 * 4);  // every epilogue warp of both CTAs
     for (int d = 0; d < 1 + kPairCopyWarps; ++d) mbar_init(&drain[d], 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -423,8 +423,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                                            __fmul_rn(__uint_as_float(r1[2 * i + 1]), alpha), kBF16);
         }
       }
+      // One arrive per warp once all its lanes' loads have completed: at CTA scope in CTA 0, and
+      // relaxed at cluster scope from CTA 1 (per-thread release arrives cost 6 us at 8192^3).
       tc_fence_before();
-      mbar_arrive_cluster(acc_empty0);
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(acc_empty);
+        else
+          mbar_arrive_relaxed_cluster(acc_empty0);
+      }
 
       const int gm = mt * kPairTileM + 128 * static_cast<int>(rank) + row;
       if (gm < p.m) {

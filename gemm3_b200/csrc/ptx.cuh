@@ -295,6 +295,13 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// The same without release semantics, for a hand-off of TMEM that this thread has finished
+// reading (tcgen05.ld followed by tcgen05.wait::ld) and ordered with
+// tcgen05.fence::before_thread_sync: no generic-proxy write needs publishing. A cluster-scope
+// release arrive costs the issuing thread 1,000-2,000 cycles on B200 while the tensor pipe is busy.
+__device__ __forceinline__ void mbar_arrive_relaxed_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 
 // TMA loads whose completion is counted on an mbarrier of either CTA of the pair.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m, int32_t x, int32_t y,

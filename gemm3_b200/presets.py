@@ -16,9 +16,11 @@ How the fields act on the B200 kernels (gemm3_b200/csrc/gemm_pair_kernel.cuh, ge
 Measured on B200 (python -m gemm3_b200.tune, BF16 out; outputs bit-identical across all):
   - the CTA-pair tile beats the one-CTA tile at every size (8192^3: 215 against 371 us; the
     one-CTA tile reads 42 % more from L2);
-  - at 16384^3 the fast_swz=2 band with cluster (8, 2) is 16 % faster than plain raster, raster
-    along M, or fast_swz 1, 4 or 8 (1579 against 1749-1890 us): it keeps the B tiles in sweep
-    resident in L2; A/SFA evict_last adds 1 %;
+  - at 16384^3 the fast_swz=2 band with cluster (8, 2) is 12-21 % faster than plain raster, raster
+    along M, or fast_swz 1, 4 or 8 (1536 against 1740-1975 us): it keeps the B tiles in sweep
+    resident in L2; A/SFA evict_last adds 1 % and B evict_first 2.6 %;
+  - at 32768^3 the band of fast_swz=2 with cluster (4, 4) beats fast_swz=4 by 5 % (14.1 against
+    14.9 ms) and B evict_first adds 3.5 %;
   - at 8192^3 and 4096^3 (operands resident in L2) raster and L2 attributes change the time by at
     most one 2-us timer step.
 Attributes with an effect: fast_swz, raster_along_m, l2_policy_{a,b,sfa,sfb},
@@ -85,6 +87,7 @@ PRESETS = {
         raster_along_m=False,
         l2_policy_a="evict_last",
         l2_policy_sfa="evict_last",
+        l2_policy_b="evict_first",
         trim_short_tail=True,
         tma_b_first=True,
         tma_sfb_first=True,
@@ -94,9 +97,10 @@ PRESETS = {
     (32768, 32768, 32768): Config.make(
         cluster=(4, 4),
         fallback=(2, 1),
-        fast_swz=4,
+        fast_swz=2,
         raster_along_m=False,
         l2_policy_a="evict_last",
+        l2_policy_b="evict_first",
         epi_store_pair=True,
         epi_store_pace_per_ktile_ns=0,
         retire_a_cols=8,
@@ -104,6 +108,22 @@ PRESETS = {
         specialize_32k=True,
     ),
 }
+
+# B200 additions: the per-GPU shapes of the N-sharded 32768^3 scaling run (N / 8, N / 4, N / 2 per
+# rank). A band of 8 CTA tiles (4 CTA-pair tiles) along M keeps the pairs in flight on the same
+# A rows while every B tile of the rank's slice stays in L2; plain raster re-streams A (17-19 %
+# slower). Keeping A resident (evict_last) and streaming B (evict_first) adds 2-5 %.
+for _n in (4096, 8192, 16384):
+    PRESETS[(32768, _n, 32768)] = Config.make(
+        cluster=(4, 1),
+        fallback=(2, 1),
+        fast_swz=2,
+        raster_along_m=False,
+        l2_policy_a="evict_last",
+        l2_policy_sfa="evict_last",
+        l2_policy_b="evict_first",
+    )
+del _n
 
 
 # B200 retune for skinny GEMMs (M <= 128, e.g. LLM projections on a few tokens): the

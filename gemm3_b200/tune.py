@@ -57,7 +57,10 @@ def candidates(m, n, k):
         variant("A and SFA evict_last", l2_policy_a="evict_last", l2_policy_sfa="evict_last")
     variant("A and SFA evict_last, persisting L2 48 MiB", persist_mb=48, l2_policy_a="evict_last",
             l2_policy_sfa="evict_last")
-    variant("B evict_first", l2_policy_b="evict_first")
+    if attrs.get("l2_policy_b") == "evict_first":
+        variant("B evict_normal", l2_policy_b=None)
+    else:
+        variant("B evict_first", l2_policy_b="evict_first")
     variant("B loads first" if not attrs.get("tma_b_first") else "A loads first",
             tma_b_first=not attrs.get("tma_b_first"))
     return out
