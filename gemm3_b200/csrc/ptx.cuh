@@ -291,14 +291,11 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
-// Arrive on an mbarrier that may live in another CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// The same without release semantics, for a hand-off of TMEM that this thread has finished
-// reading (tcgen05.ld followed by tcgen05.wait::ld) and ordered with
-// tcgen05.fence::before_thread_sync: no generic-proxy write needs publishing. A cluster-scope
-// release arrive costs the issuing thread 1,000-2,000 cycles on B200 while the tensor pipe is busy.
+// Arrive on an mbarrier that may live in another CTA of the cluster, without release semantics:
+// for a hand-off of TMEM that this thread has finished reading (tcgen05.ld followed by
+// tcgen05.wait::ld) and ordered with tcgen05.fence::before_thread_sync, where no generic-proxy
+// write needs publishing. The release form (mbarrier.arrive.release.cluster) costs the issuing
+// thread 1,000-2,000 cycles on B200 while the tensor pipe is busy.
 __device__ __forceinline__ void mbar_arrive_relaxed_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
