@@ -78,27 +78,17 @@ __device__ __constant__ float kE2M1Table[9] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0
 constexpr uint32_t kE2M1T1 = 0x3E800012u, kE2M1T2 = 0x3F3FFFF8u, kE2M1T3 = 0x3FA00005u, kE2M1T4 = 0x3FDFFFFCu,
                    kE2M1T5 = 0x40200003u, kE2M1T6 = 0x405FFFFEu, kE2M1T7 = 0x40A00002u;
 
-// d = sat(a * b + c), one rounding; sat clamps to [0, 1] (NaN -> 0).
-__device__ __forceinline__ float fma_sat(float a, float b, float c) {
-  float d;
-  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
+// kE2M1Next[c]: the reference's threshold (as bits) for rounding to code c + 1, +inf past code 7.
+__device__ __constant__ uint32_t kE2M1Next[8] = {kE2M1T1, kE2M1T2, kE2M1T3, kE2M1T4,
+                                                 kE2M1T5, kE2M1T6, kE2M1T7, 0x7F800000u};
 
-// E2M1 magnitude code (0-7) of |q| = mag by the reference's thresholds, exactly: with P = the
-// float below threshold T, the step sat(|q| * 2^100 - P * 2^100) is exactly 1 when |q| >= T (the
-// difference is at least one ulp, 2^-25, so the product is >= 2^75) and exactly 0 otherwise; the
-// code is the sum of the seven steps, accumulated on 2^23 so the float's low bits hold it.
-__device__ __forceinline__ uint32_t e2m1_mag_code_steps(float mag) {
-  float acc = 8388608.0f;
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.000022p+98f));  // T1 0x3E800012
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.7fffeep+99f));  // T2 0x3F3FFFF8
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400008p+100f)); // T3 0x3FA00005
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffff6p+100f)); // T4 0x3FDFFFFC
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400004p+101f)); // T5 0x40200003
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.bffffap+101f)); // T6 0x405FFFFE
-  acc = __fadd_rn(acc, fma_sat(mag, 0x1p100f, -0x1.400002p+102f)); // T7 0x40A00002
-  return __float_as_uint(acc) - 0x4B000000u;
+// Exact E2M1 magnitude code of |q| = mag by the reference's thresholds, given c = the
+// round-to-nearest-even code of mag * (1 - 2^-17) where that of mag * (1 + 2^-17) is c + 1: the
+// two conversions bracket the one rounding tie next to mag, and the reference moves each tie by
+// at most 18 ulps, so its code is c or c + 1, decided by one exact float comparison with the
+// threshold of code c + 1.
+__device__ __forceinline__ uint32_t e2m1_mag_code_near_tie(float mag, uint32_t c) {
+  return c + (mag >= __uint_as_float(kE2M1Next[c & 7u]) ? 1u : 0u);
 }
 
 // Hardware round-to-nearest-even of eight magnitudes to E2M1 (saturating at 6), packed two per
@@ -123,7 +113,8 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(const float (&m)[8]) {
 //    moves the boundary (within 18 ulps, relative 2.2e-6). The hardware conversions of
 //    |q| * (1 - 2^-17) and |q| * (1 + 2^-17) agree exactly when no tie lies in between, and
 //    then that code is the reference's (checked on the CPU for every float in [0, 6.5]). An
-//    element whose two conversions differ takes the exact threshold steps instead.
+//    element whose two conversions differ gets the exact code from the one threshold between
+//    them (e2m1_mag_code_near_tie).
 //  - sign: q = RN(xb / d) < 0 exactly when xb / d < -2^-150 (the tie at 2^-150 rounds to -0),
 //    i.e. when t = -xb * 2^100 - d * 2^-50 > 0; both products are exact and the FMA keeps the
 //    sign, so the bit is t's "greater than +0" test on its bit pattern (t is never -0: d > 0).
@@ -147,7 +138,8 @@ __device__ __forceinline__ uint32_t e2m1_pack8(const float* xb, float d, float r
   if (near_tie != 0u) {
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if ((near_tie >> (4 * i)) & 0xFu) w = (w & ~(0xFu << (4 * i))) | (e2m1_mag_code_steps(mag[i]) << (4 * i));
+      if ((near_tie >> (4 * i)) & 0xFu)
+        w = (w & ~(0xFu << (4 * i))) | (e2m1_mag_code_near_tie(mag[i], (w >> (4 * i)) & 0x7u) << (4 * i));
   }
   return w | neg;
 }
@@ -174,8 +166,9 @@ __device__ __forceinline__ float rcp_approx(float d) {
 //    round-to-nearest-even only within 2.2e-6 of a tie. So where the hardware conversions of lo
 //    and hi agree, no tie lies within 5e-6 of q and that code is the reference's.
 //  - An element whose two conversions differ takes the exact path: xb = RN(x * gs), the
-//    correctly rounded quotient by Markstein's correction with r = RN(1 / d), and the threshold
-//    steps. Only the magnitude bits are replaced; lo and hi carry the same sign.
+//    correctly rounded quotient by Markstein's correction with r = RN(1 / d), and the one
+//    threshold between the two codes. Only the magnitude bits are replaced; lo and hi carry the
+//    same sign.
 __device__ __forceinline__ uint32_t e2m1_pack8_fast(const float* x, float gs, float d, float clo, float chi) {
   const float2 clo2 = make_float2(clo, clo), chi2 = make_float2(chi, chi);
   float lo[8], hi[8];
@@ -199,7 +192,7 @@ __device__ __forceinline__ uint32_t e2m1_pack8_fast(const float* x, float gs, fl
         const float q1 = __fmul_rn(xb, r);
         const float rem = __fmaf_rn(q1, -d, xb);
         const float q = __fmaf_rn(rem, r, q1);
-        w = (w & ~(0x7u << (4 * i))) | (e2m1_mag_code_steps(fabsf(q)) << (4 * i));
+        w = (w & ~(0x7u << (4 * i))) | (e2m1_mag_code_near_tie(fabsf(q), (w >> (4 * i)) & 0x7u) << (4 * i));
       }
   }
   return w;

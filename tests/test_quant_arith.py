@@ -8,6 +8,9 @@ restatement (oracle/) and against IEEE division.
    E4M3 divisor significand (an exhaustive C check).
 3. The block scale through a saturating round-to-nearest-even E4M3 conversion, with values above
    464 (and NaN) sent to 0x7F by one compare, equals the reference's non-saturating encode.
+4. The two-conversion window (|q| * (1 -/+ 2^-17) rounded to nearest even) gives the reference's
+   code where both agree, and where they differ the codes are neighbours and the one threshold
+   between them gives it.
 """
 
 import os
@@ -49,18 +52,6 @@ def test_thresholds_are_the_oracles_rounding_boundaries():
                 lo = mid
         want.append(hi)
     np.testing.assert_array_equal(kernel_thresholds(), np.array(want, dtype=np.uint32))
-
-
-def test_step_constants_are_scaled_predecessors():
-    """e2m1_pack16 subtracts P * 2^100 for P = the float just below each threshold."""
-    text = open(KERNEL).read()
-    lits = re.findall(r"fma_sat\(mag, 0x1p100f, -(0x[0-9a-f.]+p\+\d+)f\)\);\s*// T(\d) (0x[0-9A-F]+)", text)
-    assert [int(k) for _, k, _ in lits] == list(range(1, 8))
-    t = kernel_thresholds()
-    for (lit, k, tbits), want in zip(lits, t):
-        assert int(tbits, 16) == int(want)
-        pred = np.uint32(int(want) - 1).view(np.float32)
-        assert float.fromhex(lit) == float(pred) * 2.0**100, (k, lit)
 
 
 def test_threshold_count_matches_oracle_codes():
@@ -109,6 +100,17 @@ def test_rne_window_fast_path_matches_reference_rounding():
     fast = lo == hi
     np.testing.assert_array_equal(lo[fast], oracle_codes(bits)[fast])
     assert fast.mean() > 0.99  # the exact fallback is rare
+    # Where they differ, the codes are neighbours and one threshold decides: the reference's code
+    # is lo's code plus (|q| >= T[lo's code + 1]), the comparison the kernel makes.
+    slow = ~fast
+    np.testing.assert_array_equal(hi[slow], lo[slow] + 1)
+    np.testing.assert_array_equal(_one_threshold_code(x[slow], lo[slow]), oracle_codes(bits)[slow])
+
+
+def _one_threshold_code(mag, lo_code):
+    """The exact path's rule: lo_code + (mag >= T[lo_code + 1]), T the kernel's thresholds."""
+    t = np.concatenate([np.zeros(1, np.uint32), kernel_thresholds()]).view(np.float32)
+    return lo_code + (np.abs(mag).astype(np.float32) >= t[np.minimum(lo_code + 1, 7)]).astype(lo_code.dtype)
 
 
 def _rne_e4m3_saturating(s):
@@ -185,6 +187,8 @@ def test_fast_path_from_raw_inputs_matches_reference():
                     clo, chi = _rne_e2m1(lo), _rne_e2m1(hi)
                     fast = clo == chi
                     np.testing.assert_array_equal(clo[fast], want[fast])
+                    np.testing.assert_array_equal(chi[~fast], clo[~fast] + 1)
+                    np.testing.assert_array_equal(_one_threshold_code(q[~fast], clo[~fast]), want[~fast])
                     checked += int(fast.sum())
                     fallback += int((~fast).sum())
     assert checked > 10 * fallback
