@@ -242,12 +242,20 @@ __device__ __forceinline__ void unpack_raw(const RawBlock<kInDtype>& rb, float (
     for (int j = 0; j < 4; ++j) {
       if constexpr (kInDtype == 2) {
         v[4 * i + j] = __uint_as_float(ws[j]);
-      } else if constexpr (kInDtype == 1) {
-        v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
-        v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
       } else {
-        v[8 * i + 2 * j] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[j] & 0xFFFFu)));
-        v[8 * i + 2 * j + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[j] >> 16)));
+        // x + (-0) with a 16-bit operand and an FP32 result (sm_100's mixed-precision add): exact,
+        // keeps the sign of zero, and runs on the FMA pipe where shifts and masks would take the
+        // ALU pipe, the kernel's busiest (8192^2 BF16: ALU instructions -11 %, 35.3 -> 34.9 us).
+        if constexpr (kInDtype == 1)
+          asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+              "add.rn.f32.bf16 %0, l, %3;\n\tadd.rn.f32.bf16 %1, h, %3;\n\t}"
+              : "=f"(v[8 * i + 2 * j]), "=f"(v[8 * i + 2 * j + 1])
+              : "r"(ws[j]), "f"(-0.0f));
+        else
+          asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+              "add.rn.f32.f16 %0, l, %3;\n\tadd.rn.f32.f16 %1, h, %3;\n\t}"
+              : "=f"(v[8 * i + 2 * j]), "=f"(v[8 * i + 2 * j + 1])
+              : "r"(ws[j]), "f"(-0.0f));
       }
     }
   }
