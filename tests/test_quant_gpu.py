@@ -224,3 +224,44 @@ def test_swizzle_matches_reference_golden(cuda_ext, golden):
 
 def test_no_device_errors(cuda_ext):
     assert cuda_ext.device_status() == 0
+
+
+def _special_16bit_rows(dtype):
+    """Rows of 16-bit inputs made of the values whose widening to FP32 needs care: signed zeros,
+    subnormals of the input type, the largest finite values, infinities and NaN, each alone in a
+    block and mixed with ordinary values."""
+    fin = torch.finfo(dtype)
+    sub = fin.tiny / 4  # a subnormal of the input type
+    rng = np.random.default_rng(17)
+    ordinary = rng.normal(size=16).astype(np.float32)
+    rows = [
+        [-0.0] * 16,
+        [0.0, -0.0] * 8,
+        [sub, -sub] * 8,
+        [sub] + [0.0] * 15,
+        [-sub, 1.0] + [-0.0] * 14,
+        [fin.max, -fin.max] + list(ordinary[:14]),
+        [float("inf")] + list(ordinary[:15]),
+        [float("-inf"), -0.0] + list(ordinary[:14]),
+        [float("nan")] + list(ordinary[:15]),
+        list(ordinary[:8]) + [-0.0, 0.0, sub, -sub, fin.tiny, -fin.tiny, 1.0, -1.0],
+        list(ordinary),
+        list(-ordinary),
+    ]
+    x = torch.tensor(rows, dtype=torch.float32).to(dtype)
+    return torch.cat([x, x.flip(1)], dim=1)  # 12 rows x 32 elements: both pair-kernel block slots
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("gs", [1.0, 448.0, 3.0e-3])
+def test_quantize_16bit_special_values_match_oracle(cuda_ext, dtype, gs):
+    """Signed zeros, subnormals, the largest finite values, infinities and NaN of 16-bit inputs,
+    through the two-block kernel (k % 32 == 0) and the one-block kernel (k = 48), bit for bit
+    against the oracle on the same values widened to FP32."""
+    x = _special_16bit_rows(dtype)
+    for xk in (x, torch.cat([x, x[:, :16]], dim=1)):
+        packed, sf_swz, sf_lin = cuda_ext.quantize_nvfp4(xk.cuda(), gs)
+        want = oracle.quantize(xk.float().numpy(), gs, div_mode=0)
+        np.testing.assert_array_equal(packed.cpu().numpy(), want[0])
+        np.testing.assert_array_equal(sf_lin.cpu().numpy(), want[2])
+        np.testing.assert_array_equal(sf_swz.cpu().numpy(), want[1])
