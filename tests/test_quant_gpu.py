@@ -197,13 +197,20 @@ def test_quantize_2pow32_elements_matches_row_slices(cuda_ext):
     torch.cuda.empty_cache()
 
 
-def test_amax_odd_sizes_and_nan(cuda_ext):
-    for n in (1, 15, 16, 17, 1000003):
-        x = torch.randn(n, device="cuda")
-        assert cuda_ext.tensor_amax(x).item() == x.abs().max().item()
-    x = torch.randn(1000, device="cuda")
-    x[123] = float("nan")
-    assert torch.isnan(cuda_ext.tensor_amax(x)).item()
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_amax_odd_sizes_and_nan(cuda_ext, dtype):
+    # sizes around the kernel's 16-byte vectors (4 or 8 elements) and its four-load unroll
+    for n in (1, 3, 7, 9, 15, 16, 17, 4095, 1000003):
+        x = torch.randn(n, device="cuda").to(dtype)
+        x[n // 2] = -7.5  # a negative maximum magnitude, anywhere in the vector stream
+        assert cuda_ext.tensor_amax(x).item() == x.float().abs().max().item()
+    for pos in (0, 123, 999):  # NaN in the vector body and in the tail
+        x = torch.randn(1003, device="cuda").to(dtype)
+        x[pos] = float("nan")
+        assert torch.isnan(cuda_ext.tensor_amax(x)).item()
+    x = torch.randn(1003, device="cuda").to(dtype)
+    x[5] = float("-inf")
+    assert cuda_ext.tensor_amax(x).item() == float("inf")
 
 
 @pytest.mark.parametrize("name", ["ties", "randn_gs_f32", "small_f16", "overflow"])
