@@ -74,6 +74,22 @@ constexpr int kPairSfColsPerStage = 4 * kPairKBlocks + 8 * kPairKBlocks;
 static_assert(kPairSfaCol + kPairSfRegions * kPairSfColsPerStage <= kTmemCols, "pair scales do not fit in TMEM");
 static_assert(kPairSmemBytes <= 232448, "pair kernel exceeds shared memory");
 
+// Epilogue drain of 32-column chunks [kC0, kC0 + kN) of one warp's accumulator rows in one TMEM
+// round trip: kN loads in flight, one wait, then x alpha and packing to FP16/BF16 pairs.
+template <int kC0, int kN, bool kBF16>
+__device__ __forceinline__ void pair_drain_chunks(uint32_t taddr, float alpha, uint32_t (&out)[kPairTileN / 2]) {
+  uint32_t r[kN][32];
+#pragma unroll
+  for (int c = 0; c < kN; ++c) tmem_ld_32x32b_x32(taddr + (kC0 + c) * 32, r[c]);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < kN; ++c)
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      out[(kC0 + c) * 16 + i] = pack_out(__fmul_rn(__uint_as_float(r[c][2 * i]), alpha),
+                                         __fmul_rn(__uint_as_float(r[c][2 * i + 1]), alpha), kBF16);
+}
+
 template <bool kBF16>
 __global__ void __launch_bounds__(kPairThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -407,22 +423,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       acc_phase ^= 1u;
       tc_fence_after();
       uint32_t out[kPairTileN / 2];
-      // Two 32-column loads in flight per wait: the MMA thread idles until the accumulator is
-      // drained, so the drain is kept to four TMEM round trips.
-#pragma unroll
-      for (int ch = 0; ch < kPairTileN / 32; ch += 2) {
-        uint32_t r0[32], r1[32];
-        tmem_ld_32x32b_x32(tmem_row + kAccCol + ch * 32, r0);
-        tmem_ld_32x32b_x32(tmem_row + kAccCol + ch * 32 + 32, r1);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          out[ch * 16 + i] = pack_out(__fmul_rn(__uint_as_float(r0[2 * i]), alpha),
-                                      __fmul_rn(__uint_as_float(r0[2 * i + 1]), alpha), kBF16);
-          out[ch * 16 + 16 + i] = pack_out(__fmul_rn(__uint_as_float(r1[2 * i]), alpha),
-                                           __fmul_rn(__uint_as_float(r1[2 * i + 1]), alpha), kBF16);
-        }
-      }
+      // The MMA thread idles until the accumulator is drained, so the drain takes three TMEM
+      // round trips (96, 96 and 64 columns), as many loads in flight per wait as the registers
+      // allow beside the packed output.
+      pair_drain_chunks<0, 3, kBF16>(tmem_row + kAccCol, alpha, out);
+      pair_drain_chunks<3, 3, kBF16>(tmem_row + kAccCol, alpha, out);
+      pair_drain_chunks<6, 2, kBF16>(tmem_row + kAccCol, alpha, out);
       // One arrive per warp once all its lanes' loads have completed: at CTA scope in CTA 0, and
       // relaxed at cluster scope from CTA 1 (per-thread release arrives cost 6 us at 8192^3).
       tc_fence_before();
