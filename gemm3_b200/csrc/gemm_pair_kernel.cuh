@@ -75,19 +75,22 @@ static_assert(kPairSfaCol + kPairSfRegions * kPairSfColsPerStage <= kTmemCols, "
 static_assert(kPairSmemBytes <= 232448, "pair kernel exceeds shared memory");
 
 // Epilogue drain of 32-column chunks [kC0, kC0 + kN) of one warp's accumulator rows in one TMEM
-// round trip: kN loads in flight, one wait, then x alpha and packing to FP16/BF16 pairs.
+// round trip: kN loads in flight, one wait, then x alpha (paired FP32 multiplies, the same IEEE
+// products as single ones) and packing to FP16/BF16 pairs.
 template <int kC0, int kN, bool kBF16>
 __device__ __forceinline__ void pair_drain_chunks(uint32_t taddr, float alpha, uint32_t (&out)[kPairTileN / 2]) {
   uint32_t r[kN][32];
 #pragma unroll
   for (int c = 0; c < kN; ++c) tmem_ld_32x32b_x32(taddr + (kC0 + c) * 32, r[c]);
   tmem_ld_wait();
+  const float2 alpha2 = make_float2(alpha, alpha);
 #pragma unroll
   for (int c = 0; c < kN; ++c)
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      out[(kC0 + c) * 16 + i] = pack_out(__fmul_rn(__uint_as_float(r[c][2 * i]), alpha),
-                                         __fmul_rn(__uint_as_float(r[c][2 * i + 1]), alpha), kBF16);
+    for (int i = 0; i < 16; ++i) {
+      const float2 v = __fmul2_rn(make_float2(__uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1])), alpha2);
+      out[(kC0 + c) * 16 + i] = pack_out(v.x, v.y, kBF16);
+    }
 }
 
 template <bool kBF16>
